@@ -1,0 +1,39 @@
+// Host-side helpers shared by the entry points: CUDA error capture, device
+// properties cache, and TMA tensor-map encoding through the driver entry point
+// (so the library needs no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dsa_b200.h"
+
+namespace dsa {
+
+// Records `e` as this thread's last CUDA error and returns DSA_ERR_CUDA, or
+// DSA_OK when e == cudaSuccess.
+int cuda_status(cudaError_t e);
+
+// Number of SMs and the max opt-in shared memory per block of the current device.
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  int major = 0;
+  int minor = 0;
+};
+int current_device_info(DeviceInfo* info);
+
+// Encodes a tiled tensor map. dims/strides follow the driver API: dims[0] is
+// the innermost extent; strides[i] (bytes) is the stride of dim i+1.
+int encode_tensor_map(CUtensorMap* tm, CUtensorMapDataType dtype, int rank, const void* base,
+                      const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                      CUtensorMapSwizzle swizzle);
+
+// Device address of the per-device error word of the current device.
+int device_error_word(unsigned int** ptr);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace dsa

@@ -1,0 +1,234 @@
+"""Lightning Indexer drop-in for the reference's Task 2 operator.
+
+Mirrors ``reference/task2_v0_ref.py`` -- ``ModelArgs``, ``Linear``,
+``ColumnParallelLinear``, ``Model(args, freqs_cis, kv_cache, compress_ratio)``,
+``forward(x, qr, start_pos, offset) -> int64``, ``_make_args``, ``get_inputs``,
+``get_init_inputs`` -- and the v1 ``ModelNew`` of ``src/task2_indexer.py:1011-1349``.
+Parameters are created in the reference's order (wq_b, then weights_proj, each
+kaiming_uniform(a=sqrt(5))) so a seeded construction yields the same weights.
+
+The forward is one call of ``dsa_indexer_fwd``: q projection + RoPE, weights
+projection, then the fused score / causal mask / top-k kernel. Indices are
+bit-exact to the rounding contract of include/dsa_b200.h, ties broken by
+ascending candidate index.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Literal, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ._native import call, lib
+
+world_size = 1
+rank = 0
+
+
+@dataclass
+class ModelArgs:
+    """Configuration object with the fields of reference/task2_v0_ref.py:21-61.
+
+    Only dim, index_n_heads, index_head_dim, rope_head_dim, index_topk and
+    q_lora_rank are read by the indexer; the other fields are kept so that code
+    written against the reference's dataclass keeps working.
+    """
+
+    max_batch_size: int = 4
+    max_seq_len: int = 4096
+    dtype: Literal["bf16", "fp8"] = "fp8"
+    scale_fmt: Literal[None, "ue8m0"] = "ue8m0"
+    expert_dtype: Literal[None, "fp4"] = None
+    scale_dtype: Literal["fp32", "fp8"] = "fp8"
+    vocab_size: int = 129280
+    dim: int = 4096
+    moe_inter_dim: int = 4096
+    n_layers: int = 7
+    n_hash_layers: int = 0
+    n_mtp_layers: int = 1
+    n_heads: int = 64
+    n_routed_experts: int = 8
+    n_shared_experts: int = 1
+    n_activated_experts: int = 2
+    score_func: Literal["softmax", "sigmoid", "sqrtsoftplus"] = "sqrtsoftplus"
+    route_scale: float = 1.0
+    swiglu_limit: float = 0.0
+    q_lora_rank: int = 1024
+    head_dim: int = 512
+    rope_head_dim: int = 64
+    norm_eps: float = 1e-6
+    o_groups: int = 8
+    o_lora_rank: int = 1024
+    window_size: int = 128
+    compress_ratios: Tuple[int, ...] = (0, 0, 4, 128, 4, 128, 4, 0)
+    compress_rope_theta: float = 40000.0
+    original_seq_len: int = 0
+    rope_theta: float = 10000.0
+    rope_factor: float = 40
+    beta_fast: int = 32
+    beta_slow: int = 1
+    index_n_heads: int = 64
+    index_head_dim: int = 128
+    index_topk: int = 512
+    hc_mult: int = 4
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+
+
+class Linear(nn.Module):
+    """Bias-free bf16 linear layer with the reference's initialisation
+    (reference/task2_v0_ref.py:63-80)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False, dtype=None):
+        super().__init__()
+        assert not bias, "the indexer's projections have no bias"
+        self.in_features = in_features
+        self.out_features = out_features
+        self.weight = nn.Parameter(torch.empty(out_features, in_features,
+                                               dtype=dtype or torch.bfloat16))
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        self.register_parameter("scale", None)
+        self.register_parameter("bias", None)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x, self.weight)
+
+
+class ColumnParallelLinear(Linear):
+    """Column-split linear (reference/task2_v0_ref.py:85-91); world_size is 1."""
+
+    def __init__(self, in_features, out_features, bias=False, dtype=None):
+        assert out_features % world_size == 0
+        self.part_out_features = out_features // world_size
+        super().__init__(in_features, self.part_out_features, bias, dtype)
+
+
+class ModelNew(nn.Module):
+    """Drop-in for ``Model`` of reference/task2_v0_ref.py:106-144."""
+
+    def __init__(self, args, freqs_cis: torch.Tensor, kv_cache: torch.Tensor,
+                 compress_ratio: int = 4):
+        super().__init__()
+        self.dim = args.dim
+        self.n_heads = args.index_n_heads
+        self.n_local_heads = args.index_n_heads // world_size
+        self.head_dim = args.index_head_dim
+        self.rope_head_dim = args.rope_head_dim
+        self.index_topk = args.index_topk
+        self.q_lora_rank = args.q_lora_rank
+        self.wq_b = ColumnParallelLinear(self.q_lora_rank, self.n_heads * self.head_dim)
+        self.weights_proj = ColumnParallelLinear(self.dim, self.n_heads, dtype=torch.bfloat16)
+        self.softmax_scale = self.head_dim ** -0.5
+        self.compress_ratio = compress_ratio
+        self.kv_cache = kv_cache
+        self.freqs_cis = freqs_cis
+        self._dev_cache = {}
+
+    # -- cached device-side operands ---------------------------------------
+    def _weights_on(self, device):
+        key = ("w", device)
+        vers = (self.wq_b.weight._version, self.weights_proj.weight._version,
+                id(self.wq_b.weight), id(self.weights_proj.weight))
+        c = self._dev_cache.get(key)
+        if c is None or c[0] != vers:
+            wq = self.wq_b.weight.detach().to(device=device, dtype=torch.bfloat16).contiguous()
+            wp = self.weights_proj.weight.detach().to(device=device,
+                                                      dtype=torch.bfloat16).contiguous()
+            c = (vers, wq, wp)
+            self._dev_cache[key] = c
+        return c[1], c[2]
+
+    def _rope_tables(self, start_pos: int, seqlen: int, device):
+        key = ("rope", start_pos, seqlen, device, id(self.freqs_cis))
+        c = self._dev_cache.get(key)
+        if c is None:
+            fc = torch.view_as_real(self.freqs_cis[start_pos:start_pos + seqlen])
+            cos = fc[..., 0].to(device=device, dtype=torch.float32).contiguous()
+            sin = fc[..., 1].to(device=device, dtype=torch.float32).contiguous()
+            c = (cos, sin)
+            self._dev_cache[key] = c
+        return c
+
+    def _workspace(self, nbytes: int, device) -> torch.Tensor:
+        key = ("ws", device)
+        c = self._dev_cache.get(key)
+        if c is None or c.numel() < nbytes:
+            c = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self._dev_cache[key] = c
+        return c
+
+    def forward(self, x: torch.Tensor, qr: torch.Tensor, start_pos: int, offset: int):
+        bsz, seqlen, _ = x.size()
+        dev = x.device
+        ratio = self.compress_ratio
+        end_pos = start_pos + seqlen
+        T = end_pos // ratio
+        K = min(self.index_topk, T)
+        assert x.is_cuda and qr.is_cuda, "inputs must be CUDA tensors"
+        assert x.dtype == torch.bfloat16 and qr.dtype == torch.bfloat16
+        assert self.n_local_heads == 16 and self.head_dim == 64, \
+            "kernel specialised to index_n_heads == 16, index_head_dim == 64"
+        assert self.rope_head_dim % 2 == 0 and self.rope_head_dim <= self.head_dim
+        assert T <= 4096 and K <= 2048, "kernel specialised to <= 4096 candidates, top-k <= 2048"
+        assert K >= 1, "need at least one candidate (end_pos >= compress_ratio)"
+        kv = self.kv_cache
+        assert kv.is_cuda and kv.dtype == torch.bfloat16 and kv.device == dev
+        assert kv.shape[0] >= bsz and kv.shape[1] >= T and kv.shape[2] == self.head_dim
+        assert kv.stride(2) == 1 and kv.stride(1) == self.head_dim, \
+            "kv_cache rows must be contiguous"
+        x = x.contiguous()
+        qr = qr.contiguous()
+        wq, wp = self._weights_on(dev)
+        cos, sin = self._rope_tables(start_pos, seqlen, dev)
+        nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim)
+        ws = self._workspace(nbytes, dev)
+        out = torch.empty(bsz, seqlen, K, dtype=torch.int64, device=dev)
+        w_scale = self.softmax_scale * self.n_heads ** -0.5
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            call("dsa_indexer_fwd", x.data_ptr(), qr.data_ptr(), wq.data_ptr(), wp.data_ptr(),
+                 cos.data_ptr(), sin.data_ptr(), kv.data_ptr(), kv.stride(0), out.data_ptr(),
+                 ws.data_ptr(), ws.numel(), bsz, seqlen, self.dim, self.q_lora_rank,
+                 self.n_heads, self.head_dim, self.rope_head_dim, self.index_topk, start_pos,
+                 ratio, offset, float(w_scale), stream)
+        return out
+
+
+def _make_args():
+    """Reference configuration (reference/task2_v0_ref.py:147-150)."""
+    return ModelArgs(max_batch_size=8, max_seq_len=2600, dim=1024, index_n_heads=16,
+                     index_head_dim=64, index_topk=128, q_lora_rank=256, rope_head_dim=32)
+
+
+def get_inputs(device: str = "cuda"):
+    a = _make_args()
+    batch_size = 8
+    seq_len = 2600
+    x = torch.randn(batch_size, seq_len, a.dim, dtype=torch.bfloat16).to(device)
+    qr = torch.randn(batch_size, seq_len, a.q_lora_rank, dtype=torch.bfloat16).to(device)
+    start_pos = 0
+    offset = 0
+    return [x, qr, start_pos, offset]
+
+
+def make_freqs_cis(rope_head_dim: int, max_seq_len: int, rope_theta: float = 10000.0,
+                   device: str = "cpu") -> torch.Tensor:
+    """freqs_cis as built by reference/task2_v0_ref.py:162-168 (complex64)."""
+    freqs = 1.0 / (rope_theta ** (torch.arange(0, rope_head_dim, 2)[:rope_head_dim // 2].float()
+                                  / rope_head_dim))
+    t = torch.arange(max_seq_len, dtype=torch.float32)
+    freqs = torch.outer(t, freqs).float().to(device)
+    return torch.polar(torch.ones_like(freqs), freqs).view(max_seq_len, -1)
+
+
+def get_init_inputs(device: str = "cuda"):
+    a = _make_args()
+    compress_ratio = 4
+    freqs_cis = make_freqs_cis(a.rope_head_dim, a.max_seq_len, 10000.0, device)
+    kv_cache = torch.randn(a.max_batch_size, a.max_seq_len // compress_ratio, a.index_head_dim,
+                           dtype=torch.bfloat16).to(device)
+    return [a, freqs_cis, kv_cache, compress_ratio]

@@ -1,0 +1,449 @@
+"""Benchmark of the B200 DeepSeek sparse-attention operator path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (per GPU): SparseAttention with
+q[8,2600,64,128] bf16, kv[8,32,128] bf16, topk_idxs[8,2600,16] int32, i.e. one
+call of the reference's Task-1 operator per step. A step is one pass of the hot
+path over one batch. Under torchrun (N > 1) every rank runs its own batch of 8
+(batch sharding, weak scaling, no collective on the data path); the time is the
+max over ranks of the CUDA-event time of the K steps.
+
+Printed (rank 0, one JSON line): value = tokens/s over all ranks, ms_per_step,
+the kernel's HBM roofline fraction (algorithmic bytes per launch / launch time,
+against MEASURED_PEAKS.json), the e2e number through the public API with the
+host->device input copies and device->host output copy inside the timed
+region, the CPU baseline (oracle port on the host cores), SM clocks sampled
+during the timed region, and per-op µs/call for the other two operators.
+
+--impl reference times the reference's algorithm on the host CPU (the C oracle
+port with all host threads) on the same workload and prints the same line with
+"impl": "reference"; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+# Workload of BASELINE configs[1] (SparseAttention), per GPU.
+B, M, H, D, NKV, TOPK = 8, 2600, 64, 128, 32, 16
+TOKENS = B * M
+SA_BYTES = (B * M * H * D * 2) * 2 + B * M * TOPK * 4 + B * NKV * D * 2 + H * 4  # 682,971,392
+METRIC = "sparse_attn tokens/s (µs/call in ms_per_step)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch of the SA kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "sparse_attn_fwd_b8_m2600.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0].replace(",", ""))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._proc = None
+
+    def __enter__(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self._proc = None
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_sa_sample(q_np, kv_np, idx_np, min_seconds: float):
+    """Oracle SA over the whole workload, repeated until min_seconds elapsed."""
+    import numpy as np
+
+    import oracle
+
+    sink = np.zeros(H, np.float32)
+    runs = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.sparse_attn(q_np, kv_np, idx_np, sink, D ** -0.5)
+        runs += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return TOKENS * runs / el, runs, el
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's algorithm on the host cores (oracle port)."""
+    import numpy as np
+
+    import oracle
+
+    if rank != 0:
+        return
+    rng = np.random.default_rng(42)
+    q = (rng.standard_normal((B, M, H, D), dtype=np.float32).view(np.uint32) >> 16).astype(
+        np.uint16)
+    kv = (rng.standard_normal((B, NKV, D), dtype=np.float32).view(np.uint32) >> 16).astype(
+        np.uint16)
+    idx = rng.integers(0, NKV, (B, M, TOPK), dtype=np.int32)
+    sink = np.zeros(H, np.float32)
+    for _ in range(args.warmup):
+        oracle.sparse_attn(q, kv, idx, sink, D ** -0.5)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.sparse_attn(q, kv, idx, sink, D ** -0.5)
+    el = time.perf_counter() - t0
+    value = TOKENS * args.steps / el
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "sparse_attn q[8,2600,64,128] kv[8,32,128] idx[8,2600,16]",
+                   "global_batch": B, "seq_len": M, "parallelism": "host cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": oracle.num_threads(),
+                         "kind": "port",
+                         "sample": f"full workload ({TOKENS} tokens) per step, C oracle, fp64"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def bench_other_ops(dev):
+    """µs/call of the Sinkhorn and Indexer operators at their reference shapes."""
+    import torch
+
+    from ascendc_kernel_b200 import sinkhorn as sk
+
+    res = {}
+    torch.manual_seed(0)
+    x = torch.randn(1, 1024, 4, 4, device=dev)
+    y = torch.empty_like(x)
+    for _ in range(20):
+        sk.sinkhorn(x, 10, 1e-6, out=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 200
+    e0.record()
+    for _ in range(n):
+        sk.sinkhorn(x, 10, 1e-6, out=y)
+    e1.record()
+    torch.cuda.synchronize()
+    res["sinkhorn"] = {"us_per_call": e0.elapsed_time(e1) * 1e3 / n,
+                       "shape": "[1,1024,4,4] fp32, repeat 10"}
+    try:
+        from ascendc_kernel_b200 import indexer as ix
+
+        torch.manual_seed(42)
+        init = ix.get_init_inputs(device=str(dev))
+        model = ix.ModelNew(*init).to(dev)
+        inp = ix.get_inputs(device=str(dev))
+        for _ in range(3):
+            model(*inp)
+        torch.cuda.synchronize()
+        n = 10
+        e0.record()
+        for _ in range(n):
+            model(*inp)
+        e1.record()
+        torch.cuda.synchronize()
+        res["indexer"] = {"us_per_call": e0.elapsed_time(e1) * 1e3 / n,
+                          "shape": "x[8,2600,1024] qr[8,2600,256] kv_cache[8,650,64] top-128"}
+    except Exception as exc:  # reported, not hidden: the indexer line says why
+        res["indexer"] = {"error": str(exc).splitlines()[0][:200]}
+    return res
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import oracle
+    from ascendc_kernel_b200 import _native
+    from ascendc_kernel_b200 import sparse_attn as sa
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    q = torch.randn(B, M, H, D, dtype=torch.bfloat16, device=dev, generator=gen)
+    kv = torch.randn(B, NKV, D, dtype=torch.bfloat16, device=dev, generator=gen)
+    idx = torch.randint(0, NKV, (B, M, TOPK), dtype=torch.int32, device=dev, generator=gen)
+    model = sa.ModelNew(H, D).to(dev)
+    sink = model.attn_sink.detach()
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        sa.sparse_attn(q, kv, sink, idx, model.softmax_scale, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)  # let the sampler start before the timed region
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        # keep the GPU busy a little longer so the sampler sees the load
+        for _ in range(max(1, 2000 // max(args.steps, 1))):
+            step()
+        torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local, world)
+    barrier(world)
+    ms_per_step = ms / args.steps
+    value = world * TOKENS * args.steps / (ms / 1e3)
+    devcode = _native.device_error(local)
+
+    peak, peak_kind = load_peaks()
+    achieved = SA_BYTES / (ms_local / args.steps / 1e3) / 1e9
+    traffic = load_traffic()
+
+    # ---- e2e through the public API: pinned host inputs, H2D + forward + D2H
+    q_h = q.cpu().pin_memory()
+    kv_h = kv.cpu().pin_memory()
+    idx_h = idx.cpu().pin_memory()
+    out_h = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    h2d = q_h.numel() * 2 + kv_h.numel() * 2 + idx_h.numel() * 4
+    d2h = out_h.numel() * 2
+
+    def e2e_step():
+        qd = q_h.to(dev, non_blocking=True)
+        kvd = kv_h.to(dev, non_blocking=True)
+        idd = idx_h.to(dev, non_blocking=True)
+        o = model(qd, kvd, idd)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_steps = max(3, min(args.steps, 10))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = world * TOKENS * e2e_steps / (e2e_ms / 1e3)
+
+    # ---- one NCCL all-gather of the outputs (assembly), reported separately
+    gather_ms = None
+    if world > 1:
+        import torch.distributed as dist
+
+        full = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
+        dist.all_gather_into_tensor(full, out)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(stream)
+        dist.all_gather_into_tensor(full, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        del full
+
+    others = bench_other_ops(dev) if rank == 0 else None
+
+    cpu = None
+    if rank == 0 and world == 1:
+        qn = q_h.view(torch.int16).numpy().view(np.uint16)
+        kvn = kv_h.view(torch.int16).numpy().view(np.uint16)
+        idn = idx_h.numpy()
+        v, runs, el = cpu_sa_sample(qn, kvn, idn, 10.0)
+        cpu = {"value": v, "unit": "tokens/s", "cores": oracle.num_threads(), "kind": "port",
+               "sample": f"full workload ({TOKENS} tokens) x {runs} run(s), {el:.1f} s, "
+                         "C oracle (fp64 gather form), all host threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (randn q/kv, uniform int32 indices), per-rank batch of 8",
+            "config": {"workload": "sparse_attn q[8,2600,64,128] kv[8,32,128] idx[8,2600,16] "
+                                   "per GPU (BASELINE configs[1])",
+                       "global_batch": B * world, "seq_len": M, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (q 340.8 MB per step)"},
+            "us_per_call": ms_per_step * 1e3,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": SA_BYTES},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "device_error_word": devcode,
+            "cpu_baseline": cpu,
+            "ops": others,
+        }
+        if gather_ms is not None:
+            line["assembly_all_gather_ms"] = gather_ms
+        print(json.dumps(line), flush=True)
+
+
+def run_profile_case(args):
+    """Small bounded case for ncu captures: W warm-up + K steps of one kernel.
+
+    --profile sa --batch 4 holds ~0.35 GB on the device (q+out 170 MB each,
+    larger than L2) and launches only the SA kernel.
+    """
+    import torch
+
+    from ascendc_kernel_b200 import sparse_attn as sa
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    b = args.batch
+    q = torch.randn(b, M, H, D, dtype=torch.bfloat16, device=dev, generator=gen)
+    kv = torch.randn(b, NKV, D, dtype=torch.bfloat16, device=dev, generator=gen)
+    idx = torch.randint(0, NKV, (b, M, TOPK), dtype=torch.int32, device=dev, generator=gen)
+    sink = torch.zeros(H, device=dev)
+    out = torch.empty_like(q)
+    for _ in range(args.warmup + args.steps):
+        sa.sparse_attn(q, kv, sink, idx, D ** -0.5, out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile, "batch": b, "launches":
+                      args.warmup + args.steps}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--profile", choices=["sa"], default=None,
+                    help="run only a bounded case of one kernel (for ncu)")
+    ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.profile:
+        run_profile_case(args)
+        return
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * dsa_b200.h -- C ABI of the B200 (sm_100a) DeepSeek sparse-attention operator
+ * path: SparseAttention, Lightning Indexer and Sinkhorn (mHC).
+ *
+ * Conventions shared by every entry point:
+ *  - All tensor arguments are raw DEVICE pointers to contiguous row-major data
+ *    (bf16 passed as `const void*`, 2 bytes per element). Sizes are element
+ *    counts. Nothing here allocates device memory; scratch is passed in.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is
+ *    asynchronous with respect to the host, like a kernel launch.
+ *  - The return value is a dsa_status_t. Argument problems are caught on the
+ *    host before any launch. A bounded device-side wait that times out does not
+ *    fail the call; it sets a code in the per-device error word, which
+ *    dsa_device_error_read() returns (after synchronizing the device).
+ *  - No entry point throws, calls exit(), or falls back to a CPU path.
+ *
+ * The reference binds each operator through pybind functions that take
+ * at::Tensor and call an `extern "C" launch_*(blockDim, stream, uint8_t* ...)`
+ * kernel launcher; the functions below take the place of those pairs.
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dsa_status {
+  DSA_OK = 0,
+  DSA_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative or inconsistent size */
+  DSA_ERR_UNSUPPORTED = 2,      /* shape outside what the kernels are built for */
+  DSA_ERR_MISALIGNED = 3,       /* a pointer or stride breaks the 16-byte TMA rule */
+  DSA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed; see dsa_last_cuda_error */
+  DSA_ERR_WORKSPACE = 5,        /* workspace pointer missing or too small */
+  DSA_ERR_NO_DEVICE = 6         /* no usable sm_100 device */
+} dsa_status_t;
+
+/* Bits of the per-device error word written by kernels (bounded waits that
+ * ran out of time, or out-of-contract data detected on the device). */
+#define DSA_DEVERR_SA_WAIT 0x0001u     /* sparse attention pipeline wait timed out */
+#define DSA_DEVERR_IX_WAIT 0x0002u     /* indexer pipeline wait timed out */
+#define DSA_DEVERR_GEMM_WAIT 0x0004u   /* projection GEMM pipeline wait timed out */
+#define DSA_DEVERR_TOPK_RANGE 0x0010u  /* top-k selection found fewer keys than expected */
+
+/* Human-readable name of a dsa_status_t value (static storage). */
+const char* dsa_status_string(int status);
+
+/* The cudaError_t of the most recent failing CUDA call made by this library
+ * on the calling thread (0 when none). */
+int dsa_last_cuda_error(void);
+
+/* Synchronizes `device`, then stores the device error word in *code_out and,
+ * when `clear` is non-zero, resets it to 0. Returns DSA_OK or DSA_ERR_CUDA. */
+int dsa_device_error_read(int device, unsigned int* code_out, int clear);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int dsa_version(void);
+
+/* ------------------------------------------------------------------------
+ * Sinkhorn (mHC) normalisation, fp32, in registers, one launch.
+ *   y = softmax(x, -1) + eps;  y /= (sum(y, -2) + eps);
+ *   repeat (repeat-1) times: y /= (sum(y, -1) + eps); y /= (sum(y, -2) + eps)
+ * x, y: [n_mat, n, n] fp32 (y may equal x). Supported: n == 4, repeat >= 1.
+ * Replaces launch_sinkhorn (src/sinkhorn_kernel.asc:175-179) and its pybind
+ * wrapper run_sinkhorn (src/task3_sinkhorn.py:227-237); semantics follow
+ * Model.forward in reference/task3_v0_ref.py:8-14.
+ */
+int dsa_sinkhorn_fwd(const float* x, float* y, int64_t n_mat, int n, int repeat, float eps,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * SparseAttention forward (multiplicity softmax, fused mm1 -> softmax -> mm2).
+ *   q      [batch, m, n_heads, head_dim] bf16
+ *   kv     [batch, n_kv, head_dim] bf16 (shared as K and V)
+ *   idx    [batch, m, topk] int32 (idx_elem_bytes 4) or int64 (8); entries < 0
+ *          or >= n_kv are masked out
+ *   sink   [n_heads] fp32 attention-sink logits
+ *   out    [batch, m, n_heads, head_dim] bf16
+ * out[b,t,h,:] = sum_j w_j kv[b, idx_j], w = softmax over the valid j of
+ * (q.kv*scale) with the sink logit in the max and the denominator.
+ * Supported: head_dim == 128, n_heads in {16,32,64,128}, 1 <= n_kv <= 32,
+ * topk*idx_elem_bytes a multiple of 16 and topk <= 256; q, kv, idx, out 16-byte aligned.
+ * Replaces launch_sa_fused (src/sparse_attn_kernel_mm.asc:310-313) and its
+ * pybind wrapper run_fused (src/task1_sparse_attn.py:420-429); semantics follow
+ * sparse_attn_ref in reference/task1_v0_ref.py:5-24.
+ */
+int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx, int idx_elem_bytes,
+                        const float* sink, void* out, int64_t batch, int64_t m, int n_heads,
+                        int head_dim, int n_kv, int topk, float softmax_scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Lightning Indexer. Rounding contract (the same in every step): each bf16
+ * result is the correctly rounded (round-to-nearest-even) value of the exact
+ * fp32/fp64 quantity it names, the same values the reference's torch ops
+ * produce up to the GEMM accumulation order.
+ *
+ * (a) q = RoPE(bf16(qr . wq_b^T)), rotation on the last rope_dim dims of every
+ *     head (interleaved pairs, fp32 non-fused a*c - b*s / a*s + b*c, one RNE).
+ *     qr [rows, q_lora_rank] bf16, wq_b [n_heads*head_dim, q_lora_rank] bf16,
+ *     cos/sin [seqlen, rope_dim/2] fp32 (position of row r is r % seqlen),
+ *     q_out [rows, n_heads*head_dim] bf16.
+ *     Replaces the aclnnMatmul executor (src/task2_indexer.py:763-809) plus
+ *     launch_ix_rope / run_rope (src/indexer_kernel_aiv.asc:110-111,
+ *     src/task2_indexer.py:724-728); semantics reference/task2_v0_ref.py:129-131.
+ */
+int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_tab,
+                           const float* sin_tab, void* q_out, int64_t rows, int q_lora_rank,
+                           int n_heads, int head_dim, int rope_dim, int64_t seqlen,
+                           void* stream);
+
+/* (b) w = bf16(bf16(x . w_proj^T) * scale).  x [rows, dim] bf16,
+ *     w_proj [n_heads, dim] bf16, w_out [rows, n_heads] bf16.
+ *     Replaces the weights_proj executor (src/task2_indexer.py:817-839);
+ *     semantics reference/task2_v0_ref.py:132. */
+int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows, int dim,
+                      int n_heads, float scale, void* stream);
+
+/* (c) Scores and top-k:
+ *     score[t,k] = bf16( sum_h bf16( relu(bf16(q[t,h].kv[k])) * w[t,h] ) )
+ *     over k < n_cand; with start_pos == 0 the causal mask drops k >= (t+1)/ratio.
+ *     out[t, 0:topk] = the candidates in descending score order, ties broken by
+ *     ascending k; masked slots are -1; valid slots hold k + offset.
+ *     q [batch*seqlen, n_heads*head_dim] bf16, w [batch*seqlen, n_heads] bf16,
+ *     kv_cache rows [k] of batch b at kv_cache + b*kv_batch_stride + k*head_dim,
+ *     out [batch*seqlen, topk] int64.
+ *     Supported: n_heads == 16, head_dim == 64, n_cand <= 4096, topk <= 2048,
+ *     topk <= n_cand.
+ *     Replaces launch_ix_fused / run_fused_t2 (src/indexer_kernel_mm.asc:434-436,
+ *     src/task2_indexer.py:730-738); semantics reference/task2_v0_ref.py:133-144.
+ */
+int dsa_indexer_score_topk(const void* q, const void* w, const void* kv_cache,
+                           int64_t kv_batch_stride, int64_t* out, int64_t batch, int64_t seqlen,
+                           int n_heads, int head_dim, int64_t n_cand, int topk, int64_t start_pos,
+                           int ratio, int64_t offset, void* stream);
+
+/* Scratch bytes dsa_indexer_fwd needs for its q and w intermediates. */
+size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim);
+
+/* (a)+(b)+(c) in one call on one stream. workspace must hold at least
+ * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) bytes, 256-byte
+ * aligned. cos/sin cover positions start_pos .. start_pos+seqlen-1.
+ * n_cand = (start_pos + seqlen) / ratio; topk = min(index_topk, n_cand).
+ * Replaces the whole ModelNew.forward path (src/task2_indexer.py:1056-1349),
+ * semantics Model.forward in reference/task2_v0_ref.py:123-144. */
+int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                    const float* cos_tab, const float* sin_tab, const void* kv_cache,
+                    int64_t kv_batch_stride, int64_t* out, void* workspace,
+                    size_t workspace_bytes, int64_t batch, int64_t seqlen, int dim,
+                    int q_lora_rank, int n_heads, int head_dim, int rope_dim, int index_topk,
+                    int64_t start_pos, int ratio, int64_t offset, float w_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */

@@ -1,0 +1,103 @@
+"""SparseAttention CUDA path vs the CPU oracle (fp64 gather form) and the
+reference's golden outputs. Tolerance: atol = rtol = 1e-2 (the reference
+harness's allclose), plus a bound on the fraction of bf16 outputs that differ
+from the correctly rounded fp64 result (the kernel keeps ~16 bits in P)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ascendc_kernel_b200 import _native
+from ascendc_kernel_b200 import sparse_attn as sa
+from tests.helpers import bf16_compare, from_u16, to_u16
+
+pytestmark = pytest.mark.gpu
+
+ATOL = RTOL = 1e-2
+MAX_MISMATCH_FRAC = 2e-3
+
+
+def run_and_compare(q, kv, idx, sink, scale, dev):
+    out = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), scale)
+    got = to_u16(out)
+    want = oracle.sparse_attn(to_u16(q), to_u16(kv), idx.numpy(), sink.numpy(), scale)
+    r = bf16_compare(got, want, ATOL, RTOL)
+    assert r["allclose"], r
+    assert r["bit_mismatch"] <= max(4, r["n"] * MAX_MISMATCH_FRAC), r
+    assert _native.device_error(dev.index) == 0
+    return r, got
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_golden(golden_dir, cuda_device, case):
+    g = np.load(os.path.join(golden_dir, "sparse_attn.npz"))
+    q = from_u16(g[f"{case}_q"])
+    kv = from_u16(g[f"{case}_kv"])
+    idx = torch.from_numpy(g[f"{case}_idx"])
+    sink = torch.from_numpy(g[f"{case}_sink"])
+    r, got = run_and_compare(q, kv, idx, sink, float(g[f"{case}_scale"]), cuda_device)
+    ref = bf16_compare(got, g[f"{case}_out"], ATOL, RTOL)
+    assert ref["allclose"], ref
+
+
+def make(b, m, h, nkv, topk, dtype=torch.int32, lo=0, seed=0, sink_std=0.0):
+    torch.manual_seed(seed)
+    q = torch.randn(b, m, h, 128, dtype=torch.bfloat16)
+    kv = torch.randn(b, nkv, 128, dtype=torch.bfloat16)
+    idx = torch.randint(lo, nkv, (b, m, topk), dtype=dtype)
+    sink = torch.randn(h) * sink_std
+    return q, kv, idx, sink
+
+
+@pytest.mark.parametrize("b,m,h,nkv,topk,dtype", [
+    (1, 1, 64, 32, 16, torch.int32),      # single token: one partial tile
+    (2, 3, 64, 32, 16, torch.int32),      # odd token count: partial last tile per batch
+    (3, 40, 16, 32, 16, torch.int64),     # 8 tokens per tile
+    (2, 17, 32, 32, 16, torch.int32),
+    (2, 9, 128, 32, 16, torch.int64),     # 1 token per tile
+    (2, 64, 64, 20, 16, torch.int32),     # n_kv < 32 (zero-filled rows)
+    (1, 50, 64, 32, 32, torch.int32),     # topk 32
+    (4, 300, 64, 32, 4, torch.int32),     # topk 4
+    (1, 700, 64, 8, 16, torch.int64),     # heavy multiplicities
+])
+def test_shapes(cuda_device, b, m, h, nkv, topk, dtype):
+    q, kv, idx, sink = make(b, m, h, nkv, topk, dtype, seed=b * 1000 + m, sink_std=1.0)
+    run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device)
+
+
+def test_masked_and_out_of_range_indices(cuda_device):
+    q, kv, idx, sink = make(2, 33, 64, 24, 16, torch.int64, lo=-3, seed=5, sink_std=2.0)
+    idx[0, 0, :] = -1            # fully masked token -> zero output
+    idx[1, 2, :] = 30            # >= n_kv: masked like a negative index
+    idx[1, 3, ::2] = 1000
+    r, got = run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device)
+    assert (got.reshape(2, 33, 64, 128)[0, 0] == 0).all()
+
+
+def test_full_reference_config(cuda_device):
+    """q[8,2600,64,128], kv[8,32,128], idx int32 [8,2600,16]."""
+    torch.manual_seed(42)
+    model = sa.ModelNew(*sa.get_init_inputs())
+    q, kv, idx = sa.get_inputs()
+    out = model.cuda()(q.to(cuda_device), kv.to(cuda_device), idx.to(cuda_device))
+    got = to_u16(out)
+    want = oracle.sparse_attn(to_u16(q), to_u16(kv), idx.numpy(), np.zeros(64, np.float32),
+                              128 ** -0.5)
+    r = bf16_compare(got, want, ATOL, RTOL)
+    print("full config vs oracle:", r)
+    assert r["allclose"], r
+    assert r["bit_mismatch"] <= r["n"] * MAX_MISMATCH_FRAC, r
+    # determinism: a second call is bit-identical
+    out2 = model(q.to(cuda_device), kv.to(cuda_device), idx.to(cuda_device))
+    assert torch.equal(out, out2)
+
+
+def test_int64_chained_indices_equal_int32(cuda_device):
+    q, kv, idx, sink = make(2, 100, 64, 32, 16, torch.int32, seed=9)
+    dev = cuda_device
+    a = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), 0.1)
+    b = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.long().to(dev), 0.1)
+    assert torch.equal(a, b)
