@@ -15,9 +15,9 @@
 //                SW128 boxes) and the tile's top-k indices into a 4-deep ring.
 //   warp 1       TMEM allocator + single-thread tcgen05 issuer:
 //                  mm1  S[128 x 32]  = Q[128 x 128] . KV^T        (8 x K16)
-//                  mm2  O[128 x 128] = P_hi . KV + P_lo . KV      (4 x K16)
-//                P is split into two bf16 halves (hi + lo) so that the
-//                weights keep ~16 significant bits through the bf16 MMA.
+//                  mm2  O[128 x 128] = (P_hi + P_mid + P_lo) . KV (6 x K16)
+//                P is split into three bf16 pieces so that the weights keep
+//                fp32-level precision (~24 bits) through the bf16 MMA.
 //   warps 2..9   two epilogue warpgroups that own alternate tiles. Each
 //                thread owns one TMEM lane (= one (token, head) row): it reads
 //                its 32 scores, forms the multiplicity softmax with the sink
@@ -42,15 +42,16 @@ constexpr int kQBoxBytes = kRows * 64 * 2;  // 16384
 constexpr int kKVBytes = kNKV * kD * 2;     // 8192
 constexpr int kKVBoxBytes = kNKV * 64 * 2;  // 4096
 constexpr int kIdxBytes = 2048;             // per stage, tpt * topk * sizeof(idx) <= 2048
-constexpr int kPBytes = kRows * kNKV * 2;   // 8192 per half
+constexpr int kPBytes = kRows * kNKV * 2;   // 8192 per piece
+constexpr int kPPieces = 3;                 // hi, mid, lo
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kStages * kQBytes;
 constexpr int kOffIdx = kOffKV + kStages * kKVBytes;
-constexpr int kOffP = kOffIdx + kStages * kIdxBytes;  // [2 wg][hi, lo]
-constexpr int kOffCnt = kOffP + 2 * 2 * kPBytes;      // [2 wg][8 tokens][32] bytes
+constexpr int kOffP = kOffIdx + kStages * kIdxBytes;  // [2 wg][hi, mid, lo]
+constexpr int kOffCnt = kOffP + 2 * kPPieces * kPBytes;  // [2 wg][8 tokens][32] bytes
 constexpr int kOffBar = kOffCnt + 2 * 8 * 32;
 constexpr int kNumBars = 2 * kStages + 5 * 2 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -166,10 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + 128u + static_cast<uint32_t>(w) * 128u;
         const uint32_t kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
-        const uint32_t phi = p_base + static_cast<uint32_t>(w) * 2u * kPBytes;
-        const uint32_t plo = phi + kPBytes;
+        const uint32_t pw = p_base + static_cast<uint32_t>(w) * kPPieces * kPBytes;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int piece = 0; piece < kPPieces; ++piece) {
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk) {
             // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
@@ -177,9 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bd = make_smem_desc(kvb + kk * 2048u, 4096u, 1024u, kLayoutSW128);
             // A = P as [M = 128] x [K = 16], K-major, no swizzle: 8x16B core
             // matrices, K-adjacent 128 B apart, M-adjacent 512 B apart.
-            const uint64_t ad = make_smem_desc((half ? plo : phi) + kk * 256u, 128u, 512u,
+            const uint64_t ad = make_smem_desc(pw + piece * kPBytes + kk * 256u, 128u, 512u,
                                                kLayoutNone);
-            umma_bf16(d, ad, bd, idesc2, (half | kk) ? 1u : 0u);
+            umma_bf16(d, ad, bd, idesc2, (piece | kk) ? 1u : 0u);
           }
         }
         umma_commit(&o_full[w]);
@@ -231,8 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float sink2 = p.sink[h] * kLog2e;
     uint8_t* cnt = smem + kOffCnt + w * 256;
-    const uint32_t p_hi = smem_u32(smem + kOffP + w * 2 * kPBytes);
-    const uint32_t p_lo = p_hi + kPBytes;
+    const uint32_t p_hi = smem_u32(smem + kOffP + w * kPPieces * kPBytes);
+    const uint32_t p_mid = p_hi + kPBytes;
+    const uint32_t p_lo = p_mid + kPBytes;
     const uint32_t prow = static_cast<uint32_t>((row >> 3) * 512 + (row & 7) * 16);
 
     // Every early exit is agreed by the whole warpgroup (named_bar_and) and
@@ -251,14 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // Multiplicity of every kv row in each token's top-k list (rows >= n_kv
       // and negative indices count as masked).
-      if (ok && t < p.tpt * 32) {
-        const int ct = t >> 5;
-        const int bin = t & 31;
+      // (token, bin) pairs: tpt * 32 of them, up to 256 for 8 tokens per tile.
+      for (int pr = t; ok && pr < p.tpt * 32; pr += 128) {
+        const int ct = pr >> 5;
+        const int bin = pr & 31;
         const IdxT* ix = reinterpret_cast<const IdxT*>(smem + kOffIdx + s * kIdxBytes) + ct * p.topk;
         int c = 0;
         if (bin < p.nkv)
           for (int j = 0; j < p.topk; ++j) c += (static_cast<long long>(ix[j]) == bin) ? 1 : 0;
-        cnt[t] = static_cast<uint8_t>(c);
+        cnt[pr] = static_cast<uint8_t>(c);
       }
       if (!named_bar_and(1 + w, 128, ok)) break;
 
@@ -297,17 +299,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = 1.0f / sum;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t hi[4], lo[4];
+          // p = hi + mid + lo exactly up to the last 8 bits of lo: each
+          // residual (p - hi, r1 - mid) is exact in fp32.
+          uint32_t hi[4], mid[4], lo[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float a0 = e[c * 8 + 2 * j] * inv;
             const float a1 = e[c * 8 + 2 * j + 1] * inv;
             hi[j] = pack_bf16x2(a0, a1);
-            const float h0 = bf16_bits_to_float(hi[j] & 0xFFFFu);
-            const float h1 = bf16_bits_to_float(hi[j] >> 16);
-            lo[j] = pack_bf16x2(a0 - h0, a1 - h1);
+            const float r0 = a0 - bf16_bits_to_float(hi[j] & 0xFFFFu);
+            const float r1 = a1 - bf16_bits_to_float(hi[j] >> 16);
+            mid[j] = pack_bf16x2(r0, r1);
+            lo[j] = pack_bf16x2(r0 - bf16_bits_to_float(mid[j] & 0xFFFFu),
+                                r1 - bf16_bits_to_float(mid[j] >> 16));
           }
           st_shared_v4(p_hi + prow + c * 128, hi[0], hi[1], hi[2], hi[3]);
+          st_shared_v4(p_mid + prow + c * 128, mid[0], mid[1], mid[2], mid[3]);
           st_shared_v4(p_lo + prow + c * 128, lo[0], lo[1], lo[2], lo[3]);
         }
         fence_proxy_async_smem();

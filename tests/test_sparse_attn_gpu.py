@@ -1,7 +1,9 @@
 """SparseAttention CUDA path vs the CPU oracle (fp64 gather form) and the
 reference's golden outputs. Tolerance: atol = rtol = 1e-2 (the reference
 harness's allclose), plus a bound on the fraction of bf16 outputs that differ
-from the correctly rounded fp64 result (the kernel keeps ~16 bits in P)."""
+from the correctly rounded fp64 result (the kernel keeps fp32-level precision
+in P through a three-piece bf16 split; the reference itself, in fp32, differs
+from fp64 in ~1e-4 of the outputs)."""
 
 import os
 
@@ -17,7 +19,7 @@ from tests.helpers import bf16_compare, from_u16, to_u16
 pytestmark = pytest.mark.gpu
 
 ATOL = RTOL = 1e-2
-MAX_MISMATCH_FRAC = 2e-3
+MAX_MISMATCH_FRAC = 1e-3
 
 
 def run_and_compare(q, kv, idx, sink, scale, dev):
