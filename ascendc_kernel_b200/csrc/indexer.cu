@@ -1,26 +1,140 @@
-// Lightning Indexer entry points (kernels added in the next step).
+// Lightning Indexer C-ABI entry points: argument checks, workspace layout and
+// the three launches (q projection + RoPE, weights projection, scores + top-k).
 #include "common.cuh"
 #include "host_util.h"
 
-extern "C" int dsa_indexer_qproj_rope(const void*, const void*, const float*, const float*, void*,
-                                      int64_t, int, int, int, int, int64_t, void*) {
-  return DSA_ERR_UNSUPPORTED;
+namespace dsa {
+int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
+                      void* q_out, int64_t rows, int K, int n_heads, int rope_dim, int64_t seqlen,
+                      cudaStream_t stream);
+int launch_wproj(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
+                 cudaStream_t stream);
+int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
+                      int64_t* out, int64_t batch, int64_t seqlen, int64_t n_cand, int topk,
+                      int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream);
+
+namespace {
+constexpr int kHeadDim = 64;
+constexpr int kScoreHeads = 16;
+constexpr int64_t kMaxCand = 1024;
+constexpr int kMaxTopk = 256;
+constexpr int64_t kMaxRowsTma = (int64_t{1} << 31) - 1;
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+int check_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
+                const void* q_out, int64_t rows, int K, int n_heads, int head_dim, int rope_dim,
+                int64_t seqlen) {
+  if (!qr || !wq || !q_out || rows < 0 || K <= 0 || n_heads <= 0 || seqlen <= 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (rope_dim < 0 || rope_dim > head_dim || (rope_dim & 1)) return DSA_ERR_INVALID_ARGUMENT;
+  if (rope_dim > 0 && (!cos_tab || !sin_tab)) return DSA_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHeadDim || K % 64 != 0 || K > 256) return DSA_ERR_UNSUPPORTED;
+  if (rows > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
+  if (!aligned16(qr) || !aligned16(wq) || !aligned16(q_out)) return DSA_ERR_MISALIGNED;
+  return DSA_OK;
 }
-extern "C" int dsa_indexer_wproj(const void*, const void*, void*, int64_t, int, int, float, void*) {
-  return DSA_ERR_UNSUPPORTED;
+
+int check_wproj(const void* x, const void* wp, const void* w_out, int64_t rows, int dim,
+                int n_heads) {
+  if (!x || !wp || !w_out || rows < 0 || dim <= 0 || n_heads <= 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (n_heads != kScoreHeads || dim % 64 != 0 || dim > 1024) return DSA_ERR_UNSUPPORTED;
+  if (rows > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(wp) || !aligned16(w_out)) return DSA_ERR_MISALIGNED;
+  return DSA_OK;
 }
-extern "C" int dsa_indexer_score_topk(const void*, const void*, const void*, int64_t, int64_t*,
-                                      int64_t, int64_t, int, int, int64_t, int, int64_t, int,
-                                      int64_t, void*) {
-  return DSA_ERR_UNSUPPORTED;
+
+int check_score(const void* q, const void* w, const void* kv, int64_t kv_bstride,
+                const int64_t* out, int64_t batch, int64_t seqlen, int n_heads, int head_dim,
+                int64_t n_cand, int topk, int64_t start_pos, int ratio) {
+  if (!q || !w || !kv || !out || batch < 0 || seqlen < 0 || n_cand < 0 || topk < 0 ||
+      start_pos < 0 || ratio <= 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (n_heads != kScoreHeads || head_dim != kHeadDim) return DSA_ERR_UNSUPPORTED;
+  if (topk > n_cand) return DSA_ERR_INVALID_ARGUMENT;
+  if (n_cand > kMaxCand || topk > kMaxTopk) return DSA_ERR_UNSUPPORTED;
+  if (kv_bstride < n_cand * kHeadDim || kv_bstride % kHeadDim != 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (batch * seqlen * kScoreHeads > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
+  if ((batch - 1) * (kv_bstride / kHeadDim) + n_cand > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(w) || !aligned16(kv) || !aligned16(out))
+    return DSA_ERR_MISALIGNED;
+  return DSA_OK;
 }
+}  // namespace
+}  // namespace dsa
+
+extern "C" int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_tab,
+                                      const float* sin_tab, void* q_out, int64_t rows,
+                                      int q_lora_rank, int n_heads, int head_dim, int rope_dim,
+                                      int64_t seqlen, void* stream) {
+  int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q_out, rows, q_lora_rank, n_heads,
+                            head_dim, rope_dim, seqlen);
+  if (st != DSA_OK || rows == 0) return st;
+  return dsa::launch_qproj_rope(qr, wq_b, cos_tab, sin_tab, q_out, rows, q_lora_rank, n_heads,
+                                rope_dim, seqlen, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows,
+                                 int dim, int n_heads, float scale, void* stream) {
+  int st = dsa::check_wproj(x, w_proj, w_out, rows, dim, n_heads);
+  if (st != DSA_OK || rows == 0) return st;
+  return dsa::launch_wproj(x, w_proj, w_out, rows, dim, scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_indexer_score_topk(const void* q, const void* w, const void* kv_cache,
+                                      int64_t kv_batch_stride, int64_t* out, int64_t batch,
+                                      int64_t seqlen, int n_heads, int head_dim, int64_t n_cand,
+                                      int topk, int64_t start_pos, int ratio, int64_t offset,
+                                      void* stream) {
+  int st = dsa::check_score(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_heads,
+                            head_dim, n_cand, topk, start_pos, ratio);
+  if (st != DSA_OK || batch == 0 || seqlen == 0 || topk == 0) return st;
+  return dsa::launch_score_topk(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_cand, topk,
+                                start_pos, ratio, offset, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads,
                                               int head_dim) {
-  return 0;
+  if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
+  const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
+  return dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2);
 }
-extern "C" int dsa_indexer_fwd(const void*, const void*, const void*, const void*, const float*,
-                               const float*, const void*, int64_t, int64_t*, void*, size_t, int64_t,
-                               int64_t, int, int, int, int, int, int, int64_t, int, int64_t, float,
-                               void*) {
-  return DSA_ERR_UNSUPPORTED;
+
+extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
+                               const void* w_proj, const float* cos_tab, const float* sin_tab,
+                               const void* kv_cache, int64_t kv_batch_stride, int64_t* out,
+                               void* workspace, size_t workspace_bytes, int64_t batch,
+                               int64_t seqlen, int dim, int q_lora_rank, int n_heads,
+                               int head_dim, int rope_dim, int index_topk, int64_t start_pos,
+                               int ratio, int64_t offset, float w_scale, void* stream) {
+  if (batch < 0 || seqlen < 0 || index_topk <= 0 || ratio <= 0 || start_pos < 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seqlen == 0) return DSA_OK;
+  const int64_t rows = batch * seqlen;
+  const int64_t n_cand = (start_pos + seqlen) / ratio;
+  const int topk = static_cast<int>(index_topk < n_cand ? index_topk : n_cand);
+  if (topk <= 0) return DSA_ERR_INVALID_ARGUMENT;
+  const size_t need = dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim);
+  if (workspace == nullptr || workspace_bytes < need ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return DSA_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* q = ws;
+  void* w = ws + dsa::align256(static_cast<size_t>(rows) * n_heads * head_dim * 2);
+  int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
+                            rope_dim, seqlen);
+  if (st != DSA_OK) return st;
+  st = dsa::check_wproj(x, w_proj, w, rows, dim, n_heads);
+  if (st != DSA_OK) return st;
+  st = dsa::check_score(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_heads, head_dim,
+                        n_cand, topk, start_pos, ratio);
+  if (st != DSA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dsa::launch_qproj_rope(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, rope_dim,
+                              seqlen, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_wproj(x, w_proj, w, rows, dim, w_scale, s);
+  if (st != DSA_OK) return st;
+  return dsa::launch_score_topk(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_cand, topk,
+                                start_pos, ratio, offset, s);
 }

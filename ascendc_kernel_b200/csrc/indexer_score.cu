@@ -1,0 +1,575 @@
+// Lightning Indexer scores + causal mask + top-k for sm_100a.
+//
+// Semantics (reference/task2_v0_ref.py:133-143), for token t of batch b:
+//   s[h,k]   = bf16(q[t,h] . kv[b,k])                (correctly rounded)
+//   e[h,k]   = bf16(relu(s[h,k]) * w[t,h])           (fp32 product, RNE)
+//   score[k] = bf16(sum_h e[h,k])                    (fp64 sum in h order, RNE)
+//   valid k  < n_r = (start_pos == 0 ? min((t+1)/ratio, T) : T)
+//   out[t]   = top-K valid k by (score desc, k asc); slots past n_r are -1,
+//              valid slots hold k + offset.
+//
+// B200 mapping (one CTA per SM, persistent; a work unit is one batch and 16
+// consecutive tokens, scheduled heaviest causal block first):
+//   warp 0      TMA: the unit's q tile (16 tokens x 16 heads = 256 rows x 64,
+//               32 KB, double buffered) and 128-row kv chunks (16 KB, 3 stages)
+//   warp 1      tcgen05: D[128 kv rows x 256 (t,h)] = KV_chunk . Q^T (K = 64)
+//               into one of two 256-column TMEM buffers
+//   warps 2..9  two epilogue warpgroups (tokens 0-7 / 8-15 of the unit). A
+//               thread owns one kv row: it loads its 16 head values per token,
+//               certifies each bf16 rounding against the accumulation bound
+//               (numerics.cuh; elements that cannot be certified are
+//               recomputed exactly by the whole warp in fp64), runs the
+//               relu / *w / head-sum chain and stores a unique 32-bit key
+//               (orderable bf16 score << 16 | 0xFFFF - k) in shared memory.
+//               After the last chunk each warp selects the top-K of two tokens
+//               with an 8-bit radix select over the keys and a register
+//               bitonic sort, and writes the int64 indices.
+#include "common.cuh"
+#include "host_util.h"
+#include "numerics.cuh"
+
+namespace dsa {
+namespace ixs {
+
+constexpr int kHeads = 16;
+constexpr int kDim = 64;
+constexpr int kTB = 16;                  // tokens per unit
+constexpr int kQRows = kTB * kHeads;     // 256
+constexpr int kChunk = 128;              // kv rows per MMA
+constexpr int kMaxT = 1024;              // candidates held in smem per token
+constexpr int kMaxK = 256;               // top-k held in registers
+constexpr int kKVStages = 3;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+
+constexpr int kQBytes = kQRows * 128;    // 32 KB
+constexpr int kKVBytes = kChunk * 128;   // 16 KB
+constexpr int kOffQ = 0;
+constexpr int kOffKV = kOffQ + 2 * kQBytes;                   // 65536
+constexpr int kOffKeys = kOffKV + kKVStages * kKVBytes;       // 114688
+constexpr int kOffQN = kOffKeys + kTB * kMaxT * 4;            // 180224
+constexpr int kOffW = kOffQN + kQRows * 4;                    // 181248
+constexpr int kOffSel = kOffW + kQRows * 4;                   // 182272: per warp hist + sel
+constexpr int kSelBytes = 256 * 4 + kMaxK * 4;                // 2 KB per warp
+constexpr int kOffBar = kOffSel + 8 * kSelBytes;              // 198656
+constexpr int kNumBars = 2 + 2 + 2 * kKVStages + 2 + 2;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmem = kOffMisc + 16 + 1024;
+
+// Accumulation bound for one K = 64 accumulator (4 MMA steps at 3 fp32 ulps
+// each, in units of ||q|| * ||kv||).
+constexpr float kGamma = 24.0f * kTwoM24 * 1.0001f;
+
+struct Params {
+  int B;
+  int64_t S;
+  int64_t T;          // candidates (end_pos / ratio)
+  int K;              // top-k (min(index_topk, T))
+  int ratio;
+  int causal;         // start_pos == 0
+  int64_t offset;
+  int n_tb;           // token blocks per batch
+  int units;
+  int64_t kv_rows_per_batch;  // kv_batch_stride / 64
+  const uint16_t* w;  // [B*S, 16]
+  int64_t* out;       // [B*S, K]
+  unsigned int* err;
+};
+
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk16) {
+  return static_cast<uint32_t>(row * 128 + ((chunk16 ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ int64_t n_valid(const Params& p, int64_t t) {
+  if (!p.causal) return p.T;
+  const int64_t n = (t + 1) / p.ratio;
+  return n < p.T ? n : p.T;
+}
+
+// Row norm (upper bound) of a 64-wide bf16 row stored SW128 in smem.
+__device__ __forceinline__ float row_norm64(const uint8_t* base, int row) {
+  float ss = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + sw128_off(row, ch));
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bf16lo_to_f32(w4[e]), hi = bf16hi_to_f32(w4[e]);
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+    }
+  }
+  return norm_upper(ss, kDim);
+}
+
+// Whole-warp exact dot product of q row `qrow` and kv row `krow` (both SW128
+// in smem): lane i multiplies dims 2i, 2i+1 in fp64, then a butterfly sum.
+__device__ __forceinline__ double warp_exact_dot(const uint8_t* qbase, int qrow,
+                                                 const uint8_t* kvbase, int krow, int lane) {
+  const int ch = lane >> 2;            // 16-byte chunk holding dims 2*lane, 2*lane+1
+  const int wo = (lane & 3) * 4;       // byte offset of the pair in the chunk
+  const uint32_t qa = *reinterpret_cast<const uint32_t*>(qbase + sw128_off(qrow, ch) + wo);
+  const uint32_t ka = *reinterpret_cast<const uint32_t*>(kvbase + sw128_off(krow, ch) + wo);
+  double s = static_cast<double>(bf16lo_to_f32(qa)) * static_cast<double>(bf16lo_to_f32(ka));
+  s = fma(static_cast<double>(bf16hi_to_f32(qa)), static_cast<double>(bf16hi_to_f32(ka)), s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  return s;
+}
+
+// Descending bitonic sort of 32*R keys held as v[r] = element r*32 + lane.
+template <int R>
+__device__ __forceinline__ void warp_bitonic_desc(uint32_t (&v)[R], int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= 32) {
+        const int rs = stride >> 5;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if ((r & rs) == 0) {
+            const int i = r * 32 + lane;
+            const bool desc_block = (i & size) == 0;  // overall descending
+            const uint32_t a = v[r], b = v[r | rs];
+            const bool swap = desc_block ? (a < b) : (a > b);
+            if (swap) {
+              v[r] = b;
+              v[r | rs] = a;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int i = r * 32 + lane;
+          const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, v[r], stride);
+          const bool lower = (i & stride) == 0;
+          const bool desc_block = (i & size) == 0;
+          // in a descending block the lower index keeps the max
+          const bool keep_max = (lower == desc_block);
+          v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
+        }
+      }
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void sort_and_store(const uint32_t* sel, int nsel, int K_out,
+                                               int64_t* out_row, int64_t offset, int lane) {
+  uint32_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < nsel ? sel[i] : 0u;
+  }
+  warp_bitonic_desc<R>(v, lane);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    if (i < K_out) {
+      out_row[i] = i < nsel ? static_cast<int64_t>(0xFFFFu - (v[r] & 0xFFFFu)) + offset
+                            : static_cast<int64_t>(-1);
+    }
+  }
+}
+
+// Top-Ksel of the n unique keys in `keys` (smem) by one warp: 8-bit radix
+// select of the Ksel-th largest key, compaction of the keys >= it, sort.
+__device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* hist, uint32_t* sel,
+                          int64_t* out_row, int64_t offset, int lane) {
+  const int ksel = n < K_out ? n : K_out;
+  uint32_t thr = 0;  // keys >= thr are selected
+  if (n > ksel) {
+    uint32_t prefix = 0, pmask = 0;
+    int need = ksel;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+      __syncwarp();
+      for (int i = lane; i < n; i += 32) {
+        const uint32_t k = keys[i];
+        if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
+      }
+      __syncwarp();
+      // lane l owns bins 255-8l .. 248-8l (descending digit order)
+      uint32_t c[8];
+      uint32_t tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - lane * 8 - j];
+        tot += c[j];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      const uint32_t excl = incl - tot;  // keys with a larger digit than my bins
+      // the lane whose range contains the crossing point finds the digit
+      int digit = -1;
+      uint32_t above = 0;
+      if (excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need)) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (digit < 0 && run + c[j] >= static_cast<uint32_t>(need)) {
+            digit = 255 - lane * 8 - j;
+            above = run;
+          }
+          run += c[j];
+        }
+      }
+      const uint32_t ball = __ballot_sync(0xFFFFFFFFu, digit >= 0);
+      const int src = __ffs(static_cast<int>(ball)) - 1;
+      digit = __shfl_sync(0xFFFFFFFFu, digit, src);
+      above = __shfl_sync(0xFFFFFFFFu, above, src);
+      need -= static_cast<int>(above);
+      prefix |= static_cast<uint32_t>(digit) << shift;
+      pmask |= 0xFFu << shift;
+      __syncwarp();
+    }
+    thr = prefix;
+  }
+  // compact the selected keys (exactly ksel of them: keys are unique)
+  int base = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const uint32_t k = i < n ? keys[i] : 0u;
+    const bool take = i < n && k >= thr;
+    const uint32_t b = __ballot_sync(0xFFFFFFFFu, take);
+    if (take) sel[base + __popc(b & ((1u << lane) - 1u))] = k;
+    base += __popc(b);
+  }
+  __syncwarp();
+  if (K_out <= 128)
+    sort_and_store<4>(sel, base, K_out, out_row, offset, lane);
+  else
+    sort_and_store<8>(sel, base, K_out, out_row, offset, lane);
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    score_topk_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_kv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;                       // [2]
+  uint64_t* q_empty = bars + 2;                  // [2], 2 arrivals (one per warpgroup)
+  uint64_t* kv_full = bars + 4;                  // [3]
+  uint64_t* kv_empty = kv_full + kKVStages;      // [3], 2 arrivals
+  uint64_t* acc_full = kv_empty + kKVStages;     // [2]
+  uint64_t* acc_empty = acc_full + 2;            // [2], 256 arrivals
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 2);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 256);
+    }
+    for (int i = 0; i < kKVStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 2);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_kv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  // unit u -> (b, token block), heaviest (latest) token blocks first
+  auto unit_of = [&](int u, int& b, int64_t& t0) {
+    b = u % p.B;
+    t0 = static_cast<int64_t>(p.n_tb - 1 - u / p.B) * kTB;
+  };
+  auto unit_chunks = [&](int64_t t0) -> int {
+    int64_t tl = t0 + kTB - 1;
+    if (tl > p.S - 1) tl = p.S - 1;
+    const int64_t nv = n_valid(p, tl);
+    return static_cast<int>((nv + kChunk - 1) / kChunk);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int lu = 0, gc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
+        int b;
+        int64_t t0;
+        unit_of(u, b, t0);
+        const int nch = unit_chunks(t0);
+        const int qb = lu & 1;
+        if (!mbar_wait(&q_empty[qb], ((lu >> 1) & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT))
+          break;
+        mbar_arrive_expect_tx(&q_full[qb], kQBytes);
+        tma_load_2d(smem + kOffQ + qb * kQBytes, &tm_q, 0,
+                    static_cast<int32_t>((static_cast<int64_t>(b) * p.S + t0) * kHeads), &q_full[qb]);
+        for (int c = 0; c < nch; ++c, ++gc) {
+          const int s = gc % kKVStages;
+          if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
+                         DSA_DEVERR_IX_WAIT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+          tma_load_2d(smem + kOffKV + s * kKVBytes, &tm_kv, 0,
+                      static_cast<int32_t>(b * p.kv_rows_per_batch + c * kChunk), &kv_full[s]);
+        }
+      }
+      if (lu > 0) mbar_drain(&q_full[(lu - 1) & 1], ((lu - 1) >> 1) & 1);
+      if (lu > 1) mbar_drain(&q_full[(lu - 2) & 1], ((lu - 2) >> 1) & 1);
+      for (int i = (gc > kKVStages ? gc - kKVStages : 0); i < gc; ++i)
+        mbar_drain(&kv_full[i % kKVStages], (i / kKVStages) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(128, kQRows, 0, 0);
+      int lu = 0, gc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
+        int b;
+        int64_t t0;
+        unit_of(u, b, t0);
+        const int nch = unit_chunks(t0);
+        const int qb = lu & 1;
+        // Every unit runs the full q-buffer handshake, even one without chunks.
+        if (!mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT)) break;
+        const uint32_t qaddr = smem_u32(smem + kOffQ + qb * kQBytes);
+        for (int c = 0; c < nch; ++c, ++gc) {
+          const int s = gc % kKVStages;
+          const int ab = gc & 1;
+          if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
+                         DSA_DEVERR_IX_WAIT) ||
+              !mbar_wait(&acc_empty[ab], ((gc >> 1) & 1) ^ 1, abort_flag, p.err,
+                         DSA_DEVERR_IX_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t kvaddr = smem_u32(smem + kOffKV + s * kKVBytes);
+#pragma unroll
+          for (int k4 = 0; k4 < kDim / 16; ++k4) {
+            const uint64_t ad = make_smem_desc(kvaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
+            const uint64_t bd = make_smem_desc(qaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
+            umma_bf16(tmem + static_cast<uint32_t>(ab) * 256u, ad, bd, idesc, k4 > 0 ? 1u : 0u);
+          }
+          umma_commit(&acc_full[ab]);
+        }
+      }
+      if (gc > 0) mbar_drain(&acc_full[(gc - 1) & 1], ((gc - 1) >> 1) & 1);
+      if (gc > 1) mbar_drain(&acc_full[(gc - 2) & 1], ((gc - 2) >> 1) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int wg = (warp - 2) >> 2;          // tokens [8 wg, 8 wg + 8) of the unit
+    const int t_in = threadIdx.x - 64 - 128 * wg;  // 0..127
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;     // kv row of the chunk = TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ew = warp - 2;                 // 0..7, selection warp id
+    float* qn = reinterpret_cast<float*>(smem + kOffQN);
+    float* wv = reinterpret_cast<float*>(smem + kOffW);
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + kOffKeys);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kOffSel + ew * kSelBytes);
+    uint32_t* sel = hist + 256;
+    bool ok = true;
+    int lu = 0, gc = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++lu) {
+      int b;
+      int64_t t0;
+      unit_of(u, b, t0);
+      const int nch = unit_chunks(t0);
+      const int qb = lu & 1;
+      const uint8_t* qs = smem + kOffQ + qb * kQBytes;
+      // (t,h) row of this thread for norms / weights: token 8wg + t_in/16, head t_in%16
+      const int qrow = wg * 128 + t_in;
+      {
+        const int64_t tok = t0 + (qrow >> 4);
+        float wf = 0.f;
+        if (tok < p.S)
+          wf = bf16lo_to_f32(p.w[(static_cast<int64_t>(b) * p.S + tok) * kHeads + (qrow & 15)]);
+        wv[qrow] = wf;
+      }
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err,
+                                             DSA_DEVERR_IX_WAIT));
+      if (ok) qn[qrow] = row_norm64(qs, qrow);
+      // Early exits below always fall through to the CTA-wide barrier 3, which
+      // both warpgroups reach the same number of times.
+      ok = named_bar_and(1 + wg, 128, ok);
+      for (int c = 0; ok && c < nch; ++c, ++gc) {
+        const int s = gc % kKVStages;
+        const int ab = gc & 1;
+        const uint8_t* kvs = smem + kOffKV + s * kKVBytes;
+        const int k = c * kChunk + row;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag,
+                                               p.err, DSA_DEVERR_IX_WAIT));
+        if (ok)
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[ab], (gc >> 1) & 1, abort_flag, p.err,
+                                                 DSA_DEVERR_IX_WAIT));
+        if (ok) {
+          tc_fence_after();
+          const float kvn = row_norm64(kvs, row) * kGamma;
+#pragma unroll 1
+          for (int tl = 0; tl < 8; ++tl) {
+            const int tt = wg * 8 + tl;            // token slot in the unit
+            const int64_t tok = t0 + tt;
+            const int64_t nv = tok < p.S ? n_valid(p, tok) : 0;
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tmem + lane_off + static_cast<uint32_t>(ab * 256 + tt * 16), r);
+            const bool active = k < nv;
+            // certify the 16 bf16 dot products of this (token, kv row)
+            uint32_t sb[16];
+            uint32_t fl = 0;
+#pragma unroll
+            for (int h = 0; h < 16; ++h) {
+              const float v = __uint_as_float(r[h]);
+              const float E = qn[tt * 16 + h] * kvn;
+              sb[h] = 0;
+              if (v < -E) continue;  // certainly negative: relu makes it 0
+              if (!certified_bf16(v, E, &sb[h])) fl |= 1u << h;
+            }
+            if (!active) fl = 0;
+            uint32_t any = __ballot_sync(0xFFFFFFFFu, fl != 0);
+            while (any) {
+              const int L = __ffs(static_cast<int>(any)) - 1;
+              any &= any - 1;
+              uint32_t m = __shfl_sync(0xFFFFFFFFu, fl, L);
+              const int kL = __shfl_sync(0xFFFFFFFFu, row, L);
+              while (m) {
+                const int h = __ffs(static_cast<int>(m)) - 1;
+                m &= m - 1;
+                const double d = warp_exact_dot(qs, tt * 16 + h, kvs, kL, lane);
+                if (lane == L) {
+                  const uint32_t bits = round_f64_to_bf16(d);
+#pragma unroll
+                  for (int j = 0; j < 16; ++j)
+                    if (j == h) sb[j] = bits;
+                }
+              }
+            }
+            if (active) {
+              double acc = 0.0;
+#pragma unroll
+              for (int h = 0; h < 16; ++h) {
+                float sv = __uint_as_float(sb[h] << 16);
+                sv = sv > 0.f ? sv : 0.f;  // relu, -0 -> +0
+                const float e =
+                    __uint_as_float(f32_to_bf16_rne(__fmul_rn(sv, wv[tt * 16 + h])) << 16);
+                acc += static_cast<double>(e);
+              }
+              uint32_t tb = round_f64_to_bf16(acc);
+              if (tb == 0x8000u) tb = 0;
+              const uint32_t ord = (tb & 0x8000u) ? (~tb & 0xFFFFu) : (tb | 0x8000u);
+              keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[ab]);
+        }
+        ok = named_bar_and(1 + wg, 128, ok);
+        if (ok && t_in == 0) mbar_arrive(&kv_empty[s]);
+      }
+      if (ok && t_in == 0) mbar_arrive(&q_empty[qb]);
+      // all keys of the unit are written
+      if (!named_bar_and(3, 256, ok)) break;
+      for (int tt = ew * 2; tt < ew * 2 + 2; ++tt) {
+        const int64_t tok = t0 + tt;
+        if (tok >= p.S) continue;
+        const int64_t nv = n_valid(p, tok);
+        int64_t* out_row = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
+        warp_topk(keys + tt * kMaxT, static_cast<int>(nv), p.K, hist, sel, out_row, p.offset,
+                  lane);
+      }
+      if (!named_bar_and(3, 256, ok)) break;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace ixs
+
+int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
+                      int64_t* out, int64_t batch, int64_t seqlen, int64_t n_cand, int topk,
+                      int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream) {
+  using namespace ixs;
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st != DSA_OK) return st;
+  if (di.max_smem_optin < kSmem) return DSA_ERR_UNSUPPORTED;
+  unsigned int* err = nullptr;
+  st = device_error_word(&err);
+  if (st != DSA_OK) return st;
+  CUtensorMap tm_q, tm_kv;
+  {
+    const uint64_t dims[2] = {kDim, static_cast<uint64_t>(batch * seqlen * kHeads)};
+    const uint64_t strides[1] = {kDim * 2};
+    const uint32_t box[2] = {kDim, kQRows};
+    st = encode_tensor_map(&tm_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DSA_OK) return st;
+  }
+  const int64_t rows_per_batch = kv_bstride / kDim;
+  {
+    const uint64_t rows = static_cast<uint64_t>((batch - 1) * rows_per_batch + n_cand);
+    const uint64_t dims[2] = {kDim, rows};
+    const uint64_t strides[1] = {kDim * 2};
+    const uint32_t box[2] = {kDim, kChunk};
+    st = encode_tensor_map(&tm_kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DSA_OK) return st;
+  }
+  Params p;
+  p.B = static_cast<int>(batch);
+  p.S = seqlen;
+  p.T = n_cand;
+  p.K = topk;
+  p.ratio = ratio;
+  p.causal = start_pos == 0 ? 1 : 0;
+  p.offset = offset;
+  p.n_tb = static_cast<int>((seqlen + kTB - 1) / kTB);
+  p.units = p.n_tb * p.B;
+  p.kv_rows_per_batch = rows_per_batch;
+  p.w = static_cast<const uint16_t*>(w);
+  p.out = out;
+  p.err = err;
+  static bool attr_done[64] = {false};
+  if (!attr_done[di.device]) {
+    st = cuda_status(cudaFuncSetAttribute(score_topk_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    if (st != DSA_OK) return st;
+    attr_done[di.device] = true;
+  }
+  const int grid = p.units < di.num_sms ? p.units : di.num_sms;
+  score_topk_kernel<<<grid, kThreads, kSmem, stream>>>(tm_q, tm_kv, p);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace dsa

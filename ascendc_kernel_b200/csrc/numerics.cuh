@@ -1,0 +1,70 @@
+// Rounding helpers shared by the Lightning Indexer kernels.
+//
+// Contract: every bf16 that the indexer produces from a dot product is the
+// round-to-nearest-even value of the exact dot product ("correct rounding").
+// The tensor cores deliver an fp32 approximation v with |v - exact| <= E for a
+// bound E computed from operand norms (see certified_bf16); when the interval
+// [v - E, v + E] cannot contain a bf16 rounding boundary, RNE(v) is the
+// correctly rounded result. Otherwise the element is recomputed as an fp64 sum
+// of the exact products in ascending index order and rounded with
+// round_f64_to_bf16 -- the same arithmetic as the CPU oracle.
+//
+// Error model of the tensor-core accumulator (measured on B200 for bf16
+// inputs, fp32 accumulate, K in {64, 256, 1024}, random, wide-range and
+// same-sign data): each K=16 MMA step adds at most ~0.5 fp32 ulp of the sum of
+// the magnitudes accumulated so far. The kernels use twice that, per step, and
+// bound the sum of magnitudes by ||a|| * ||b|| (Cauchy-Schwarz).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace dsa {
+
+constexpr float kTwoM23 = 1.1920928955078125e-07f;  // 2^-23
+constexpr float kTwoM24 = 5.9604644775390625e-08f;  // 2^-24
+
+// RNE of a finite fp32 to bf16 bits.
+__device__ __forceinline__ uint32_t f32_to_bf16_rne(float v) {
+  uint32_t u = __float_as_uint(v);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+// Correctly rounded fp64 -> bf16 bits: round to odd into fp32 (24 bits), then
+// RNE into bf16 (8 bits); 24 >= 8 + 2 makes the double rounding exact.
+__device__ __forceinline__ uint32_t round_f64_to_bf16(double d) {
+  float f = __double2float_rz(d);
+  if (static_cast<double>(f) != d) f = __uint_as_float(__float_as_uint(f) | 1u);
+  return f32_to_bf16_rne(f);
+}
+
+// Certified rounding. v: fp32 approximation of an exact real x with
+// |v - x| <= E. Returns true and the bf16 bits of RNE(x) in *bits when that
+// can be decided from v alone, false when x may lie on the other side of a
+// rounding boundary (the caller then recomputes x exactly).
+__device__ __forceinline__ bool certified_bf16(float v, float E, uint32_t* bits) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ex = u & 0x7F800000u;
+  // Need a normal v well away from 0 and from the fp32 exponent limits.
+  if (ex < (9u << 23) || ex >= (0xFEu << 23)) return false;
+  if (!(fabsf(v) > E)) return false;
+  // bf16 ulp at v: 2^(e-7). Within the binade of v the only RNE boundary in
+  // the bf16 interval [t, t + ulp) that contains v is m = t + ulp/2; the
+  // boundaries of the neighbouring intervals are >= ulp/4 away.
+  const float ulp = __uint_as_float(ex - (7u << 23));
+  if (!(E < 0.25f * ulp)) return false;
+  const float m = __uint_as_float((u & 0xFFFF0000u) | 0x8000u);
+  if (!(fabsf(v - m) > E)) return false;  // exact subtraction (Sterbenz)
+  *bits = f32_to_bf16_rne(v);
+  return true;
+}
+
+// Upper bound of sqrt(sum of squares) accumulated in fp32 as `ss`, n terms.
+__device__ __forceinline__ float norm_upper(float ss, int n) {
+  return sqrtf(ss * (1.0f + static_cast<float>(n + 4) * kTwoM24)) * (1.0f + 4.0f * kTwoM24);
+}
+
+__device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+}  // namespace dsa

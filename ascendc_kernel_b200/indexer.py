@@ -173,7 +173,7 @@ class ModelNew(nn.Module):
         assert self.n_local_heads == 16 and self.head_dim == 64, \
             "kernel specialised to index_n_heads == 16, index_head_dim == 64"
         assert self.rope_head_dim % 2 == 0 and self.rope_head_dim <= self.head_dim
-        assert T <= 4096 and K <= 2048, "kernel specialised to <= 4096 candidates, top-k <= 2048"
+        assert T <= 1024 and K <= 256, "kernel specialised to <= 1024 candidates, top-k <= 256"
         assert K >= 1, "need at least one candidate (end_pos >= compress_ratio)"
         kv = self.kv_cache
         assert kv.is_cuda and kv.dtype == torch.bfloat16 and kv.device == dev
@@ -196,6 +196,54 @@ class ModelNew(nn.Module):
                  self.n_heads, self.head_dim, self.rope_head_dim, self.index_topk, start_pos,
                  ratio, offset, float(w_scale), stream)
         return out
+
+
+def qproj_rope(qr: torch.Tensor, wq: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+               n_heads: int, head_dim: int, rope_dim: int, seqlen: int) -> torch.Tensor:
+    """q = RoPE(bf16(qr @ wq.T)) with correctly rounded bf16 (dsa_indexer_qproj_rope).
+
+    qr [rows, q_lora_rank] bf16, wq [n_heads*head_dim, q_lora_rank] bf16,
+    cos/sin [seqlen, rope_dim/2] fp32 (row r at position r % seqlen).
+    """
+    qr = qr.contiguous()
+    rows = qr.numel() // qr.shape[-1]
+    out = torch.empty(rows, n_heads * head_dim, dtype=torch.bfloat16, device=qr.device)
+    stream = torch.cuda.current_stream(qr.device).cuda_stream
+    with torch.cuda.device(qr.device):
+        call("dsa_indexer_qproj_rope", qr.data_ptr(), wq.contiguous().data_ptr(),
+             cos.contiguous().data_ptr(), sin.contiguous().data_ptr(), out.data_ptr(), rows,
+             qr.shape[-1], n_heads, head_dim, rope_dim, seqlen, stream)
+    return out
+
+
+def wproj(x: torch.Tensor, wp: torch.Tensor, scale: float) -> torch.Tensor:
+    """w = bf16(bf16(x @ wp.T) * scale) with correct rounding (dsa_indexer_wproj)."""
+    x = x.contiguous()
+    rows = x.numel() // x.shape[-1]
+    out = torch.empty(rows, wp.shape[0], dtype=torch.bfloat16, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        call("dsa_indexer_wproj", x.data_ptr(), wp.contiguous().data_ptr(), out.data_ptr(), rows,
+             x.shape[-1], wp.shape[0], float(scale), stream)
+    return out
+
+
+def score_topk(q: torch.Tensor, w: torch.Tensor, kv_cache: torch.Tensor, batch: int,
+               seqlen: int, n_cand: int, topk: int, start_pos: int, ratio: int,
+               offset: int) -> torch.Tensor:
+    """Scores, causal mask and top-k indices (dsa_indexer_score_topk).
+
+    q [batch*seqlen, 16*64] bf16, w [batch*seqlen, 16] bf16, kv_cache [>=batch, >=n_cand, 64]
+    bf16 with contiguous rows. Returns int64 [batch, seqlen, topk].
+    """
+    assert kv_cache.stride(2) == 1 and kv_cache.stride(1) == kv_cache.shape[2]
+    out = torch.empty(batch, seqlen, topk, dtype=torch.int64, device=q.device)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    with torch.cuda.device(q.device):
+        call("dsa_indexer_score_topk", q.contiguous().data_ptr(), w.contiguous().data_ptr(),
+             kv_cache.data_ptr(), kv_cache.stride(0), out.data_ptr(), batch, seqlen, 16, 64,
+             n_cand, topk, start_pos, ratio, offset, stream)
+    return out
 
 
 def _make_args():

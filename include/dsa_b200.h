@@ -102,6 +102,8 @@ int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx, int idx_
  *     qr [rows, q_lora_rank] bf16, wq_b [n_heads*head_dim, q_lora_rank] bf16,
  *     cos/sin [seqlen, rope_dim/2] fp32 (position of row r is r % seqlen),
  *     q_out [rows, n_heads*head_dim] bf16.
+ *     Supported: head_dim == 64, q_lora_rank a multiple of 64 and <= 256,
+ *     rope_dim even and <= head_dim.
  *     Replaces the aclnnMatmul executor (src/task2_indexer.py:763-809) plus
  *     launch_ix_rope / run_rope (src/indexer_kernel_aiv.asc:110-111,
  *     src/task2_indexer.py:724-728); semantics reference/task2_v0_ref.py:129-131.
@@ -113,6 +115,7 @@ int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_ta
 
 /* (b) w = bf16(bf16(x . w_proj^T) * scale).  x [rows, dim] bf16,
  *     w_proj [n_heads, dim] bf16, w_out [rows, n_heads] bf16.
+ *     Supported: n_heads == 16, dim a multiple of 64 and <= 1024.
  *     Replaces the weights_proj executor (src/task2_indexer.py:817-839);
  *     semantics reference/task2_v0_ref.py:132. */
 int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows, int dim,
@@ -126,8 +129,8 @@ int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t ro
  *     q [batch*seqlen, n_heads*head_dim] bf16, w [batch*seqlen, n_heads] bf16,
  *     kv_cache rows [k] of batch b at kv_cache + b*kv_batch_stride + k*head_dim,
  *     out [batch*seqlen, topk] int64.
- *     Supported: n_heads == 16, head_dim == 64, n_cand <= 4096, topk <= 2048,
- *     topk <= n_cand.
+ *     Supported: n_heads == 16, head_dim == 64, n_cand <= 1024, topk <= 256,
+ *     topk <= n_cand; kv_batch_stride a multiple of 64 and >= n_cand*64.
  *     Replaces launch_ix_fused / run_fused_t2 (src/indexer_kernel_mm.asc:434-436,
  *     src/task2_indexer.py:730-738); semantics reference/task2_v0_ref.py:133-144.
  */

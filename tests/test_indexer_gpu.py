@@ -1,0 +1,166 @@
+"""Lightning Indexer CUDA path vs the CPU oracle: every stage bit-exact, the
+final int64 indices equal with torch.equal (canonical tie order: descending
+score, ascending index)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ascendc_kernel_b200 import _native
+from ascendc_kernel_b200 import indexer as ix
+from tests.helpers import from_u16, to_u16
+
+pytestmark = pytest.mark.gpu
+
+
+def golden(golden_dir, p):
+    g = np.load(os.path.join(golden_dir, "indexer.npz"))
+    meta = [int(v) for v in g[p + "meta"]]
+    keys = ["batch", "seqlen", "start_pos", "offset", "ratio", "dim", "qlora", "nh", "hd", "rd",
+            "topk"]
+    return g, dict(zip(keys, meta))
+
+
+@pytest.mark.parametrize("p", ["p_", "d_"])
+def test_projections_bit_exact_golden(golden_dir, cuda_device, p):
+    g, c = golden(golden_dir, p)
+    dev = cuda_device
+    B, S = c["batch"], c["seqlen"]
+    q = ix.qproj_rope(from_u16(g[p + "qr"], dev).reshape(B * S, -1), from_u16(g[p + "wq"], dev),
+                      torch.from_numpy(g[p + "cos"]).to(dev), torch.from_numpy(g[p + "sin"]).to(dev),
+                      c["nh"], c["hd"], c["rd"], S)
+    want_q = oracle.rope(oracle.linear_bf16(g[p + "qr"].reshape(B * S, -1), g[p + "wq"]),
+                         g[p + "cos"], g[p + "sin"], c["nh"], c["hd"], c["rd"], S)
+    assert np.array_equal(to_u16(q), want_q)
+    w = ix.wproj(from_u16(g[p + "x"], dev).reshape(B * S, -1), from_u16(g[p + "wp"], dev),
+                 float(g[p + "w_scale"]))
+    want_w = oracle.scale_bf16(oracle.linear_bf16(g[p + "x"].reshape(B * S, -1), g[p + "wp"]),
+                               float(g[p + "w_scale"]))
+    assert np.array_equal(to_u16(w), want_w)
+    assert _native.device_error(dev.index) == 0
+
+
+def _model_from_golden(g, c, p, dev):
+    args = ix.ModelArgs(max_batch_size=c["batch"], max_seq_len=64, dim=c["dim"],
+                        index_n_heads=c["nh"], index_head_dim=c["hd"], index_topk=c["topk"],
+                        q_lora_rank=c["qlora"], rope_head_dim=c["rd"])
+    freqs = ix.make_freqs_cis(c["rd"], 64)
+    kv = from_u16(g[p + "kv"], dev)
+    m = ix.ModelNew(args, freqs, kv, c["ratio"])
+    with torch.no_grad():
+        m.wq_b.weight.copy_(from_u16(g[p + "wq"]))
+        m.weights_proj.weight.copy_(from_u16(g[p + "wp"]))
+    return m
+
+
+@pytest.mark.parametrize("p", ["p_", "d_"])
+def test_forward_golden_equals_oracle(golden_dir, cuda_device, p):
+    g, c = golden(golden_dir, p)
+    dev = cuda_device
+    m = _model_from_golden(g, c, p, dev)
+    # the rope table built here equals the generator's (same formula, same ops)
+    fc = torch.view_as_real(m.freqs_cis[c["start_pos"]:c["start_pos"] + c["seqlen"]])
+    assert np.array_equal(fc[..., 0].numpy(), g[p + "cos"])
+    x = from_u16(g[p + "x"], dev)
+    qr = from_u16(g[p + "qr"], dev)
+    got = m(x, qr, c["start_pos"], c["offset"])
+    want = oracle.indexer_fwd(g[p + "x"], g[p + "qr"], g[p + "wq"], g[p + "wp"], g[p + "cos"],
+                              g[p + "sin"], g[p + "kv"], n_heads=c["nh"], head_dim=c["hd"],
+                              rope_dim=c["rd"], index_topk=c["topk"], start_pos=c["start_pos"],
+                              ratio=c["ratio"], offset=c["offset"],
+                              w_scale=float(g[p + "w_scale"]))
+    assert torch.equal(got.cpu(), torch.from_numpy(want))
+    # against the reference itself: same value lists wherever the scores agree
+    # (checked in the CPU oracle tests); here at least the -1 layout matches
+    assert torch.equal((got.cpu() < 0), torch.from_numpy(g[p + "idx"] < 0))
+
+
+def _random_case(batch, seqlen, start_pos, offset, ratio, topk, dim=256, qlora=128, tcache=None,
+                 seed=0, kv_scale=1.0, dev=None, ties=False):
+    torch.manual_seed(seed)
+    T = (start_pos + seqlen) // ratio
+    tc = tcache or T
+    args = ix.ModelArgs(max_batch_size=batch, max_seq_len=start_pos + seqlen, dim=dim,
+                        index_n_heads=16, index_head_dim=64, index_topk=topk, q_lora_rank=qlora,
+                        rope_head_dim=32)
+    freqs = ix.make_freqs_cis(32, start_pos + seqlen)
+    kv = (torch.randn(batch, tc, 64) * kv_scale).to(torch.bfloat16)
+    if ties:  # few distinct kv rows -> many exactly equal scores
+        kv = kv[:, torch.randint(0, 3, (tc,))].contiguous()
+    m = ix.ModelNew(args, freqs, kv.to(dev), ratio)
+    x = torch.randn(batch, seqlen, dim, dtype=torch.bfloat16)
+    qr = torch.randn(batch, seqlen, qlora, dtype=torch.bfloat16)
+    if ties:
+        qr = qr.round().to(torch.bfloat16)
+    got = m(x.to(dev), qr.to(dev), start_pos, offset)
+    fc = torch.view_as_real(freqs[start_pos:start_pos + seqlen])
+    want = oracle.indexer_fwd(to_u16(x), to_u16(qr), to_u16(m.wq_b.weight),
+                              to_u16(m.weights_proj.weight), fc[..., 0].contiguous().numpy(),
+                              fc[..., 1].contiguous().numpy(), to_u16(kv), n_heads=16,
+                              head_dim=64, rope_dim=32, index_topk=topk, start_pos=start_pos,
+                              ratio=ratio, offset=offset,
+                              w_scale=64 ** -0.5 * 16 ** -0.5)
+    return got.cpu(), torch.from_numpy(want)
+
+
+@pytest.mark.parametrize("batch,seqlen,start_pos,offset,ratio,topk", [
+    (1, 37, 0, 0, 4, 8),        # ragged token block, K = min(8, 9)
+    (2, 100, 0, 7, 4, 32),      # K = topk < T
+    (1, 64, 0, 0, 4, 64),       # K = T: every token short of candidates
+    (3, 50, 0, 0, 1, 16),       # ratio 1
+    (2, 200, 0, 0, 2, 128),     # two kv chunks
+    (2, 40, 24, 3, 4, 8),       # decode: no causal mask, + offset
+    (1, 1, 99, 0, 4, 16),       # single-token decode
+    (2, 600, 0, 0, 1, 256),     # 600 candidates, top-256
+])
+def test_forward_shapes_equal_oracle(cuda_device, batch, seqlen, start_pos, offset, ratio, topk):
+    got, want = _random_case(batch, seqlen, start_pos, offset, ratio, topk,
+                             seed=seqlen + start_pos, dev=cuda_device)
+    assert torch.equal(got, want)
+    assert _native.device_error(cuda_device.index) == 0
+
+
+def test_larger_cache_stride_and_dims(cuda_device):
+    got, want = _random_case(2, 96, 0, 0, 4, 16, dim=1024, qlora=256, tcache=40, seed=3,
+                             dev=cuda_device)
+    assert torch.equal(got, want)
+
+
+def test_heavy_ties_use_ascending_index(cuda_device):
+    got, want = _random_case(2, 300, 0, 0, 4, 32, seed=11, dev=cuda_device, ties=True)
+    assert torch.equal(got, want)
+
+
+def test_full_reference_config(cuda_device):
+    """BASELINE configs[2] with the reference's seeded construction: x[8,2600,1024],
+    qr[8,2600,256], kv_cache[8,650,64], top-128; indices equal to the oracle's."""
+    torch.manual_seed(42)
+    args, freqs_cis, kv_cache, ratio = ix.get_init_inputs(device="cpu")
+    model = ix.ModelNew(args, freqs_cis, kv_cache.to(cuda_device), ratio)
+    x, qr, start_pos, offset = ix.get_inputs(device="cpu")
+    got = model(x.to(cuda_device), qr.to(cuda_device), start_pos, offset)
+    fc = torch.view_as_real(freqs_cis[:2600])
+    want, inter = oracle.indexer_fwd(
+        to_u16(x), to_u16(qr), to_u16(model.wq_b.weight), to_u16(model.weights_proj.weight),
+        fc[..., 0].contiguous().numpy(), fc[..., 1].contiguous().numpy(), to_u16(kv_cache),
+        n_heads=16, head_dim=64, rope_dim=32, index_topk=128, start_pos=0, ratio=4, offset=0,
+        w_scale=model.softmax_scale * model.n_heads ** -0.5, want_intermediates=True)
+    # stage by stage first, so a failure names the stage
+    dev = cuda_device
+    q = ix.qproj_rope(qr.to(dev).reshape(-1, 256), model.wq_b.weight.to(dev),
+                      fc[..., 0].contiguous().to(dev), fc[..., 1].contiguous().to(dev), 16, 64,
+                      32, 2600)
+    assert np.array_equal(to_u16(q), inter["q"]), int((to_u16(q) != inter["q"]).sum())
+    w = ix.wproj(x.to(dev).reshape(-1, 1024), model.weights_proj.weight.to(dev),
+                 model.softmax_scale * model.n_heads ** -0.5)
+    assert np.array_equal(to_u16(w), inter["w"]), int((to_u16(w) != inter["w"]).sum())
+    got_c = got.cpu()
+    mism_rows = int((got_c != torch.from_numpy(want)).any(dim=-1).sum())
+    assert torch.equal(got_c, torch.from_numpy(want)), f"{mism_rows} rows differ"
+    # determinism
+    again = model(x.to(dev), qr.to(dev), start_pos, offset)
+    assert torch.equal(got, again)
+    assert _native.device_error(dev.index) == 0
