@@ -401,6 +401,19 @@ def run_profile_case(args):
     from ascendc_kernel_b200 import sparse_attn as sa
 
     dev = torch.device("cuda", 0)
+    if args.profile == "ix":
+        from ascendc_kernel_b200 import indexer as ix
+
+        torch.manual_seed(42)
+        init = ix.get_init_inputs(device=str(dev))
+        model = ix.ModelNew(*init)
+        inp = ix.get_inputs(device=str(dev))
+        for _ in range(args.warmup + args.steps):
+            model(*inp)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "ix", "batch": 8, "launches":
+                          3 * (args.warmup + args.steps)}))
+        return
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)
     b = args.batch
@@ -422,7 +435,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()
