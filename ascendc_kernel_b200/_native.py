@@ -41,6 +41,10 @@ SIGNATURES = {
                                _c_void_p, _i64, _c_void_p, _c_void_p, _size_t, _i64, _i64, _i32,
                                _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i64, _f32,
                                _c_void_p]),
+    "dsa_indexer_fwd_noalloc": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                       _c_void_p, _c_void_p, _i64, _c_void_p, _i64, _i64, _i32,
+                                       _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i64, _f32,
+                                       _c_void_p]),
 }
 
 _LIB = None

@@ -155,6 +155,26 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
                     int q_lora_rank, int n_heads, int head_dim, int rope_dim, int index_topk,
                     int64_t start_pos, int ratio, int64_t offset, float w_scale, void* stream);
 
+/* dsa_indexer_fwd for callers that cannot allocate device memory at call
+ * time -- plug-ins whose host framework owns all device memory and forbids
+ * allocating inside an operator, or latency-critical paths where a
+ * cudaMalloc/cudaFree (which can synchronize the device) is not acceptable.
+ * Same arguments and result as dsa_indexer_fwd, without the workspace: the q
+ * and w intermediates live in a fixed 48 MiB array inside the library, one per
+ * device that loads it, held until the process exits. The request needs
+ * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) <= 48 MiB,
+ * i.e. at most 24,197 tokens (batch*seqlen) at 16 heads x 64 dims; larger
+ * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
+ * device looks up the array's address; make it before any stream capture.
+ * Every call on a device uses the same array, so calls that overlap on the GPU
+ * race. This entry point has no counterpart in the reference. */
+int dsa_indexer_fwd_noalloc(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                            const float* cos_tab, const float* sin_tab, const void* kv_cache,
+                            int64_t kv_batch_stride, int64_t* out, int64_t batch, int64_t seqlen,
+                            int dim, int q_lora_rank, int n_heads, int head_dim, int rope_dim,
+                            int index_topk, int64_t start_pos, int ratio, int64_t offset,
+                            float w_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
