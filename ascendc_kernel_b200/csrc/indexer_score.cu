@@ -50,8 +50,12 @@ constexpr int kOffKeys = kOffKV + kKVStages * kKVBytes;       // 114688
 constexpr int kOffQN = kOffKeys + kTB * kMaxT * 4;            // 180224
 constexpr int kOffW = kOffQN + kQRows * 4;                    // 181248
 constexpr int kOffSel = kOffW + kQRows * 4;                   // 182272: per warp hist + sel
-constexpr int kSelBytes = 256 * 4 + kMaxK * 4;                // 2 KB per warp
-constexpr int kOffBar = kOffSel + 8 * kSelBytes;              // 198656
+constexpr int kHistCopies = 4;                                // lanes spread over copies
+constexpr int kSelBytes = kHistCopies * 256 * 4 + kMaxK * 4;  // 5 KB per warp
+constexpr int kOffNV = kOffSel + 8 * kSelBytes;               // 223232: [16] int
+constexpr int kOffWP = kOffNV + kTB * 4;                      // [256] w as bf16x2 {w, w}
+constexpr int kOffPS = kOffWP + kQRows * 4;                   // [256] prmt selector
+constexpr int kOffBar = kOffPS + kQRows * 4;
 constexpr int kNumBars = 2 + 2 + 2 * kKVStages + 2 + 2;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmem = kOffMisc + 16 + 1024;
@@ -103,19 +107,104 @@ __device__ __forceinline__ float row_norm64(const uint8_t* base, int row) {
   return norm_upper(ss, kDim);
 }
 
-// Whole-warp exact dot product of q row `qrow` and kv row `krow` (both SW128
-// in smem): lane i multiplies dims 2i, 2i+1 in fp64, then a butterfly sum.
-__device__ __forceinline__ double warp_exact_dot(const uint8_t* qbase, int qrow,
-                                                 const uint8_t* kvbase, int krow, int lane) {
-  const int ch = lane >> 2;            // 16-byte chunk holding dims 2*lane, 2*lane+1
-  const int wo = (lane & 3) * 4;       // byte offset of the pair in the chunk
-  const uint32_t qa = *reinterpret_cast<const uint32_t*>(qbase + sw128_off(qrow, ch) + wo);
-  const uint32_t ka = *reinterpret_cast<const uint32_t*>(kvbase + sw128_off(krow, ch) + wo);
-  double s = static_cast<double>(bf16lo_to_f32(qa)) * static_cast<double>(bf16lo_to_f32(ka));
-  s = fma(static_cast<double>(bf16hi_to_f32(qa)), static_cast<double>(bf16hi_to_f32(ka)), s);
+// Exact dot product of q row `qrow` and kv row `krow` (both SW128 in smem):
+// exact fp64 products summed in ascending dimension order (the oracle's
+// order), rounded once to bf16.
+__device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qrow,
+                                                   const uint8_t* kvbase, int krow) {
+  double acc = 0.0;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-  return s;
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint4 a = *reinterpret_cast<const uint4*>(qbase + sw128_off(qrow, ch));
+    const uint4 b = *reinterpret_cast<const uint4*>(kvbase + sw128_off(krow, ch));
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc = fma(static_cast<double>(bf16lo_to_f32(aw[e])), static_cast<double>(bf16lo_to_f32(bw[e])),
+                acc);
+      acc = fma(static_cast<double>(bf16hi_to_f32(aw[e])), static_cast<double>(bf16hi_to_f32(bw[e])),
+                acc);
+    }
+  }
+  return round_f64_to_bf16(acc);
+}
+
+// score key of candidate k from its 16 correctly rounded bf16 head scores:
+// e_h = bf16(relu(s_h) * w_h), score = bf16(sum_h e_h) (pairwise fp64; the 16
+// terms have 8 significant bits, so the sum is exact like the oracle's),
+// key = orderable score << 16 | (0xFFFF - k), -0 treated as +0.
+__device__ __forceinline__ uint32_t score_key(const uint32_t (&sb)[16], const float (&wf)[16],
+                                              int k) {
+  double e[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) {
+    const float sv = fmaxf(__uint_as_float(sb[h] << 16), 0.f);
+    e[h] = static_cast<double>(__uint_as_float(f32_to_bf16_rne(__fmul_rn(sv, wf[h])) << 16));
+  }
+#pragma unroll
+  for (int st = 1; st < 16; st <<= 1)
+#pragma unroll
+    for (int h = 0; h < 16; h += 2 * st) e[h] += e[h + st];
+  uint32_t tb = round_f64_to_bf16(e[0]);
+  if (tb == 0x8000u) tb = 0;
+  const uint32_t ord = (tb & 0x8000u) ? (~tb & 0xFFFFu) : (tb | 0x8000u);
+  return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+}
+
+__device__ __forceinline__ void load_token_vectors(const float* qn, const float* wv, int tt,
+                                                   float (&qv)[16], float (&wf)[16]) {
+#pragma unroll
+  for (int h4 = 0; h4 < 4; ++h4) {
+    const float4 a = reinterpret_cast<const float4*>(qn + tt * 16)[h4];
+    const float4 c = reinterpret_cast<const float4*>(wv + tt * 16)[h4];
+    qv[4 * h4 + 0] = a.x; qv[4 * h4 + 1] = a.y; qv[4 * h4 + 2] = a.z; qv[4 * h4 + 3] = a.w;
+    wf[4 * h4 + 0] = c.x; wf[4 * h4 + 1] = c.y; wf[4 * h4 + 2] = c.z; wf[4 * h4 + 3] = c.w;
+  }
+}
+
+// Per-warp queue of (token, kv row) pairs whose score could not be certified.
+// Entry: word 0 = token slot << 16 | kv row in the chunk, word 1 = mask of the
+// heads whose bf16 score is uncertain, words 2..9 = the 16 head scores as bf16
+// pairs (exact for the heads not in the mask).
+constexpr int kRqWords = 10;
+
+// One lane per queued pair: exact recomputation of the uncertain heads, then
+// the exact score chain; writes the key.
+__device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
+                                         const uint8_t* kvs, const float* wv, uint32_t* keys,
+                                         int chunk_base, int lane) {
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) {
+    uint32_t* e = rq + i * kRqWords;
+    const int tt = static_cast<int>(e[0] >> 16);
+    const int row = static_cast<int>(e[0] & 0xFFFFu);
+    uint32_t m = e[1];
+#pragma unroll 1
+    while (m) {
+      const int h = __ffs(static_cast<int>(m)) - 1;
+      m &= m - 1;
+      const uint32_t bits = exact_dot_bits(qs, tt * 16 + h, kvs, row);
+      const uint32_t w2 = e[2 + (h >> 1)];
+      e[2 + (h >> 1)] = (h & 1) ? ((w2 & 0xFFFFu) | (bits << 16)) : ((w2 & 0xFFFF0000u) | bits);
+    }
+    uint32_t sb[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t w2 = e[2 + j];
+      sb[2 * j] = w2 & 0xFFFFu;
+      sb[2 * j + 1] = w2 >> 16;
+    }
+    float wf[16];
+#pragma unroll
+    for (int h4 = 0; h4 < 4; ++h4) {
+      const float4 c = reinterpret_cast<const float4*>(wv + tt * 16)[h4];
+      wf[4 * h4 + 0] = c.x; wf[4 * h4 + 1] = c.y; wf[4 * h4 + 2] = c.z; wf[4 * h4 + 3] = c.w;
+    }
+    const int k = chunk_base + row;
+    keys[tt * kMaxT + k] = score_key(sb, wf, k);
+  }
+  __syncwarp();
 }
 
 // Descending bitonic sort of 32*R keys held as v[r] = element r*32 + lane.
@@ -185,14 +274,17 @@ __device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* hist
   if (n > ksel) {
     uint32_t prefix = 0, pmask = 0;
     int need = ksel;
+    // The leading key bits (sign and exponent of similar scores) take few
+    // values, so lanes spread their atomics over kHistCopies histograms.
+    uint32_t* my_hist = hist + (lane & (kHistCopies - 1)) * 256;
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+      for (int j = 0; j < 8 * kHistCopies; ++j) hist[lane * 8 * kHistCopies + j] = 0;
       __syncwarp();
       for (int i = lane; i < n; i += 32) {
         const uint32_t k = keys[i];
-        if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
+        if ((k & pmask) == prefix) atomicAdd(&my_hist[(k >> shift) & 0xFFu], 1u);
       }
       __syncwarp();
       // lane l owns bins 255-8l .. 248-8l (descending digit order)
@@ -200,7 +292,10 @@ __device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* hist
       uint32_t tot = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - lane * 8 - j];
+        const int bin = 255 - lane * 8 - j;
+        c[j] = 0;
+#pragma unroll
+        for (int cp = 0; cp < kHistCopies; ++cp) c[j] += hist[cp * 256 + bin];
         tot += c[j];
       }
       uint32_t incl = tot;
@@ -392,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* wv = reinterpret_cast<float*>(smem + kOffW);
     uint32_t* keys = reinterpret_cast<uint32_t*>(smem + kOffKeys);
     uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kOffSel + ew * kSelBytes);
-    uint32_t* sel = hist + 256;
+    uint32_t* sel = hist + kHistCopies * 256;
     bool ok = true;
     int lu = 0, gc = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++lu) {
@@ -404,12 +499,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* qs = smem + kOffQ + qb * kQBytes;
       // (t,h) row of this thread for norms / weights: token 8wg + t_in/16, head t_in%16
       const int qrow = wg * 128 + t_in;
+      int* nvs = reinterpret_cast<int*>(smem + kOffNV);
+      if (t_in < 8) {
+        const int64_t tok = t0 + wg * 8 + t_in;
+        nvs[wg * 8 + t_in] = tok < p.S ? static_cast<int>(n_valid(p, tok)) : 0;
+      }
       {
         const int64_t tok = t0 + (qrow >> 4);
-        float wf = 0.f;
-        if (tok < p.S)
-          wf = bf16lo_to_f32(p.w[(static_cast<int64_t>(b) * p.S + tok) * kHeads + (qrow & 15)]);
-        wv[qrow] = wf;
+        uint32_t wb = 0;
+        if (tok < p.S) wb = p.w[(static_cast<int64_t>(b) * p.S + tok) * kHeads + (qrow & 15)];
+        wv[qrow] = bf16lo_to_f32(wb);
+        reinterpret_cast<uint32_t*>(smem + kOffWP)[qrow] = wb | (wb << 16);
+        // an interval times a negative weight swaps its ends
+        reinterpret_cast<uint32_t*>(smem + kOffPS)[qrow] = (wb & 0x8000u) ? 0x1032u : 0x3210u;
       }
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err,
                                              DSA_DEVERR_IX_WAIT));
@@ -430,60 +532,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
           tc_fence_after();
           const float kvn = row_norm64(kvs, row) * kGamma;
+          // the selection scratch of this warp is idle during the chunk phase:
+          // it holds the queue of pairs that need an exact recomputation
+          uint32_t* rq = hist;
+          constexpr int kRqCap = kSelBytes / 4 / kRqWords;
+          const uint32_t* wpk = reinterpret_cast<const uint32_t*>(smem + kOffWP);
+          const uint32_t* psel = reinterpret_cast<const uint32_t*>(smem + kOffPS);
+          int rq_n = 0;
 #pragma unroll 1
-          for (int tl = 0; tl < 8; ++tl) {
-            const int tt = wg * 8 + tl;            // token slot in the unit
-            const int64_t tok = t0 + tt;
-            const int64_t nv = tok < p.S ? n_valid(p, tok) : 0;
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + static_cast<uint32_t>(ab * 256 + tt * 16), r);
-            const bool active = k < nv;
-            // certify the 16 bf16 dot products of this (token, kv row)
-            uint32_t sb[16];
-            uint32_t fl = 0;
+          for (int tl = 0; tl < 8; tl += 2) {
+            // two tokens per TMEM load: 32 columns = 2 tokens x 16 heads
+            const int tt0 = wg * 8 + tl;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem + lane_off + static_cast<uint32_t>(ab * 256 + tt0 * 16), r);
 #pragma unroll
-            for (int h = 0; h < 16; ++h) {
-              const float v = __uint_as_float(r[h]);
-              const float E = qn[tt * 16 + h] * kvn;
-              sb[h] = 0;
-              if (v < -E) continue;  // certainly negative: relu makes it 0
-              if (!certified_bf16(v, E, &sb[h])) fl |= 1u << h;
-            }
-            if (!active) fl = 0;
-            uint32_t any = __ballot_sync(0xFFFFFFFFu, fl != 0);
-            while (any) {
-              const int L = __ffs(static_cast<int>(any)) - 1;
-              any &= any - 1;
-              uint32_t m = __shfl_sync(0xFFFFFFFFu, fl, L);
-              const int kL = __shfl_sync(0xFFFFFFFFu, row, L);
-              while (m) {
-                const int h = __ffs(static_cast<int>(m)) - 1;
-                m &= m - 1;
-                const double d = warp_exact_dot(qs, tt * 16 + h, kvs, kL, lane);
-                if (lane == L) {
-                  const uint32_t bits = round_f64_to_bf16(d);
+            for (int j = 0; j < 2; ++j) {
+              const int tt = tt0 + j;
+              const bool active = k < nvs[tt];
+              // Each head score s_h is known to lie in [v - E, v + E]; carry the
+              // interval [RNE(v-E), RNE(v+E)] through relu, *w (bf16 RNE, both
+              // monotone) and the head sum (fp32, rounded outward). If both ends
+              // of the sum round to the same bf16, that is the exact score.
+              float slo[4] = {0.f, 0.f, 0.f, 0.f}, shi[4] = {0.f, 0.f, 0.f, 0.f};
+              uint32_t unc = 0, lob[8];
 #pragma unroll
-                  for (int j = 0; j < 16; ++j)
-                    if (j == h) sb[j] = bits;
+              for (int h4 = 0; h4 < 4; ++h4) {
+                const float4 qv4 = reinterpret_cast<const float4*>(qn + tt * 16)[h4];
+                const uint4 wp4 = reinterpret_cast<const uint4*>(wpk + tt * 16)[h4];
+                const uint4 ps4 = reinterpret_cast<const uint4*>(psel + tt * 16)[h4];
+                const float qva[4] = {qv4.x, qv4.y, qv4.z, qv4.w};
+                const uint32_t wpa[4] = {wp4.x, wp4.y, wp4.z, wp4.w};
+                const uint32_t psa[4] = {ps4.x, ps4.y, ps4.z, ps4.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int h = h4 * 4 + i;
+                  const float v = __uint_as_float(r[j * 16 + h]);
+                  const float E = __fmul_ru(qva[i], kvn);
+                  uint32_t pr;  // upper half RNE(v+E), lower half RNE(v-E)
+                  asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+                      : "=r"(pr)
+                      : "f"(__fadd_ru(v, E)), "f"(__fsub_rd(v, E)));
+                  const uint32_t lo16 = pr & 0xFFFFu, hi16 = pr >> 16;
+                  // uncertain: the ends differ and the upper end is positive
+                  const bool hipos = hi16 != 0u && !(hi16 & 0x8000u);
+                  unc |= (lo16 != hi16 && hipos) ? (1u << h) : 0u;
+                  if (h & 1) lob[h >> 1] |= lo16 << 16; else lob[h >> 1] = lo16;
+                  uint32_t e2 = __byte_perm(pr, 0, psa[i]);
+                  asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
+                  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
+                  slo[i] = __fadd_rd(slo[i], bf16lo_to_f32(e2));
+                  shi[i] = __fadd_ru(shi[i], bf16hi_to_f32(e2));
                 }
               }
-            }
-            if (active) {
-              double acc = 0.0;
+              const float lo_sum = __fadd_rd(__fadd_rd(slo[0], slo[1]), __fadd_rd(slo[2], slo[3]));
+              const float hi_sum = __fadd_ru(__fadd_ru(shi[0], shi[1]), __fadd_ru(shi[2], shi[3]));
+              uint32_t tp;
+              asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(tp) : "f"(hi_sum), "f"(lo_sum));
+              uint32_t tlo = tp & 0xFFFFu, thi = tp >> 16;
+              if (tlo == 0x8000u) tlo = 0;  // -0 == +0
+              if (thi == 0x8000u) thi = 0;
+              const bool need = active && tlo != thi;
+              const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
+              if (bal) {
+                if (rq_n + __popc(bal) > kRqCap) {
+                  drain_queue(rq, rq_n, qs, kvs, wv, keys, c * kChunk, lane);
+                  rq_n = 0;
+                }
+                if (need) {
+                  uint32_t* e = rq + (rq_n + __popc(bal & ((1u << lane) - 1u))) * kRqWords;
+                  e[0] = (static_cast<uint32_t>(tt) << 16) | static_cast<uint32_t>(row);
+                  e[1] = unc;
 #pragma unroll
-              for (int h = 0; h < 16; ++h) {
-                float sv = __uint_as_float(sb[h] << 16);
-                sv = sv > 0.f ? sv : 0.f;  // relu, -0 -> +0
-                const float e =
-                    __uint_as_float(f32_to_bf16_rne(__fmul_rn(sv, wv[tt * 16 + h])) << 16);
-                acc += static_cast<double>(e);
+                  for (int q2 = 0; q2 < 8; ++q2) e[2 + q2] = lob[q2];
+                }
+                rq_n += __popc(bal);
               }
-              uint32_t tb = round_f64_to_bf16(acc);
-              if (tb == 0x8000u) tb = 0;
-              const uint32_t ord = (tb & 0x8000u) ? (~tb & 0xFFFFu) : (tb | 0x8000u);
-              keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+              if (active && !need) {
+                const uint32_t ord = (tlo & 0x8000u) ? (~tlo & 0xFFFFu) : (tlo | 0x8000u);
+                keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+              }
             }
           }
+          if (rq_n > 0) drain_queue(rq, rq_n, qs, kvs, wv, keys, c * kChunk, lane);
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
         }

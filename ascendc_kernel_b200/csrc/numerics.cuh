@@ -42,21 +42,15 @@ __device__ __forceinline__ uint32_t round_f64_to_bf16(double d) {
 // |v - x| <= E. Returns true and the bf16 bits of RNE(x) in *bits when that
 // can be decided from v alone, false when x may lie on the other side of a
 // rounding boundary (the caller then recomputes x exactly).
+// RNE is monotone, so if lo = v - E (rounded down) and hi = v + E (rounded up)
+// have the same RNE, every x in [lo, hi] rounds to it. *bits is RNE(lo).
 __device__ __forceinline__ bool certified_bf16(float v, float E, uint32_t* bits) {
-  const uint32_t u = __float_as_uint(v);
-  const uint32_t ex = u & 0x7F800000u;
-  // Need a normal v well away from 0 and from the fp32 exponent limits.
-  if (ex < (9u << 23) || ex >= (0xFEu << 23)) return false;
-  if (!(fabsf(v) > E)) return false;
-  // bf16 ulp at v: 2^(e-7). Within the binade of v the only RNE boundary in
-  // the bf16 interval [t, t + ulp) that contains v is m = t + ulp/2; the
-  // boundaries of the neighbouring intervals are >= ulp/4 away.
-  const float ulp = __uint_as_float(ex - (7u << 23));
-  if (!(E < 0.25f * ulp)) return false;
-  const float m = __uint_as_float((u & 0xFFFF0000u) | 0x8000u);
-  if (!(fabsf(v - m) > E)) return false;  // exact subtraction (Sterbenz)
-  *bits = f32_to_bf16_rne(v);
-  return true;
+  const float lo = __fsub_rd(v, E);
+  const float hi = __fadd_ru(v, E);
+  uint32_t pair;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pair) : "f"(hi), "f"(lo));
+  *bits = pair & 0xFFFFu;
+  return (pair >> 16) == (pair & 0xFFFFu);
 }
 
 // Upper bound of sqrt(sum of squares) accumulated in fp32 as `ss`, n terms.
