@@ -119,37 +119,21 @@ class ClockSampler:
 
 
 def dist_setup():
-    import torch
-    import torch.distributed as dist
+    from ascendc_kernel_b200 import dist as dd
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        torch.cuda.set_device(local)
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    return world, rank, local
+    return dd.init(backend="nccl", timeout_s=120.0)
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from ascendc_kernel_b200 import dist as dd
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return dd.max_over_ranks(x)
 
 
 def barrier(world: int):
-    if world > 1:
-        import torch.distributed as dist
+    from ascendc_kernel_b200 import dist as dd
 
-        dist.barrier()
+    dd.barrier()
 
 
 def cpu_sa_sample(q_np, kv_np, idx_np, min_seconds: float):
@@ -337,14 +321,13 @@ def run_ours(args, world, rank, local):
     # ---- one NCCL all-gather of the outputs (assembly), reported separately
     gather_ms = None
     if world > 1:
-        import torch.distributed as dist
+        from ascendc_kernel_b200 import dist as dd
 
-        full = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
-        dist.all_gather_into_tensor(full, out)
+        full = dd.gather_batch(out, B * world)
         torch.cuda.synchronize()
         barrier(world)
         e0.record(stream)
-        dist.all_gather_into_tensor(full, out)
+        full = dd.gather_batch(out, B * world)
         e1.record(stream)
         torch.cuda.synchronize()
         gather_ms = max_over_ranks(e0.elapsed_time(e1), world)
