@@ -6,7 +6,12 @@
 namespace dsa {
 int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
                       void* q_out, int64_t rows, int K, int n_heads, int rope_dim, int64_t seqlen,
-                      cudaStream_t stream);
+                      const void* a_slices, const int* a_sig, const float* a_err,
+                      const float* a_n3, const void* b_slices, const int* b_sig,
+                      const float* b_err, const float* b_n3, const int* a_span,
+                      const int* b_span, uint32_t* open_bits, cudaStream_t stream);
+int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* sig, float* err,
+                     float* n3, int* span, cudaStream_t stream);
 int launch_wproj(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
                  cudaStream_t stream);
 int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
@@ -16,11 +21,62 @@ int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_b
 namespace {
 constexpr int kHeadDim = 64;
 constexpr int kScoreHeads = 16;
+constexpr int kMaxQprojHeads = 16;
 constexpr int64_t kMaxCand = 1024;
 constexpr int kMaxTopk = 256;
 constexpr int64_t kMaxRowsTma = (int64_t{1} << 31) - 1;
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Front part of the workspace: the int8 slices of wq_b and of qr for the q
+// projection (indexer_split.cu), 3 planes each, sized for q_lora_rank <= 256,
+// with the per-row exponent, remainder bound, ||S3|| and bit span, and the
+// bitmask of output elements left to the exact fix-up.
+struct SliceRegion {
+  size_t b_slices, b_sig, b_err, b_n3, b_span, a_slices, a_sig, a_err, a_n3, a_span, open, bytes;
+};
+constexpr size_t kMaxQLora = 256;
+SliceRegion slice_region(int n_heads, int head_dim, int64_t rows) {
+  const size_t N = static_cast<size_t>(n_heads) * head_dim;
+  const size_t R = static_cast<size_t>(rows);
+  SliceRegion r;
+  r.b_slices = 0;
+  r.b_sig = r.b_slices + align256(3 * N * kMaxQLora);
+  r.b_err = r.b_sig + align256(N * 4);
+  r.b_n3 = r.b_err + align256(N * 4);
+  r.b_span = r.b_n3 + align256(N * 4);
+  r.a_slices = r.b_span + align256(N * 4);
+  r.a_sig = r.a_slices + align256(3 * R * kMaxQLora);
+  r.a_err = r.a_sig + align256(R * 4);
+  r.a_n3 = r.a_err + align256(R * 4);
+  r.a_span = r.a_n3 + align256(R * 4);
+  r.open = r.a_span + align256(R * 4);
+  r.bytes = r.open + align256(R * (N / 8));
+  return r;
+}
+
+// Slices wq_b and qr into the workspace, then runs the q projection.
+int run_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
+              void* q_out, int64_t rows, int K, int n_heads, int head_dim, int rope_dim,
+              int64_t seqlen, uint8_t* ws, cudaStream_t s) {
+  const SliceRegion r = slice_region(n_heads, head_dim, rows);
+  int* b_sig = reinterpret_cast<int*>(ws + r.b_sig);
+  float* b_err = reinterpret_cast<float*>(ws + r.b_err);
+  float* b_n3 = reinterpret_cast<float*>(ws + r.b_n3);
+  int* a_sig = reinterpret_cast<int*>(ws + r.a_sig);
+  float* a_err = reinterpret_cast<float*>(ws + r.a_err);
+  float* a_n3 = reinterpret_cast<float*>(ws + r.a_n3);
+  int* b_span = reinterpret_cast<int*>(ws + r.b_span);
+  int* a_span = reinterpret_cast<int*>(ws + r.a_span);
+  int st = launch_row_split(wq, static_cast<int64_t>(n_heads) * head_dim, K, ws + r.b_slices,
+                            b_sig, b_err, b_n3, b_span, s);
+  if (st == DSA_OK)
+    st = launch_row_split(qr, rows, K, ws + r.a_slices, a_sig, a_err, a_n3, a_span, s);
+  if (st != DSA_OK) return st;
+  return launch_qproj_rope(qr, wq, cos_tab, sin_tab, q_out, rows, K, n_heads, rope_dim, seqlen,
+                           ws + r.a_slices, a_sig, a_err, a_n3, ws + r.b_slices, b_sig, b_err,
+                           b_n3, a_span, b_span, reinterpret_cast<uint32_t*>(ws + r.open), s);
+}
 
 int check_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
                 const void* q_out, int64_t rows, int K, int n_heads, int head_dim, int rope_dim,
@@ -29,7 +85,8 @@ int check_qproj(const void* qr, const void* wq, const float* cos_tab, const floa
     return DSA_ERR_INVALID_ARGUMENT;
   if (rope_dim < 0 || rope_dim > head_dim || (rope_dim & 1)) return DSA_ERR_INVALID_ARGUMENT;
   if (rope_dim > 0 && (!cos_tab || !sin_tab)) return DSA_ERR_INVALID_ARGUMENT;
-  if (head_dim != kHeadDim || K % 64 != 0 || K > 256) return DSA_ERR_UNSUPPORTED;
+  if (head_dim != kHeadDim || K % 64 != 0 || K > 256 || n_heads > kMaxQprojHeads)
+    return DSA_ERR_UNSUPPORTED;
   if (rows > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
   if (!aligned16(qr) || !aligned16(wq) || !aligned16(q_out)) return DSA_ERR_MISALIGNED;
   return DSA_OK;
@@ -66,12 +123,17 @@ int check_score(const void* q, const void* w, const void* kv, int64_t kv_bstride
 extern "C" int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_tab,
                                       const float* sin_tab, void* q_out, int64_t rows,
                                       int q_lora_rank, int n_heads, int head_dim, int rope_dim,
-                                      int64_t seqlen, void* stream) {
+                                      int64_t seqlen, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
   int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q_out, rows, q_lora_rank, n_heads,
                             head_dim, rope_dim, seqlen);
   if (st != DSA_OK || rows == 0) return st;
-  return dsa::launch_qproj_rope(qr, wq_b, cos_tab, sin_tab, q_out, rows, q_lora_rank, n_heads,
-                                rope_dim, seqlen, static_cast<cudaStream_t>(stream));
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
+      workspace_bytes < dsa::slice_region(n_heads, head_dim, rows).bytes)
+    return DSA_ERR_WORKSPACE;
+  return dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q_out, rows, q_lora_rank, n_heads, head_dim,
+                        rope_dim, seqlen, static_cast<uint8_t*>(workspace),
+                        static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows,
@@ -97,7 +159,8 @@ extern "C" size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int
                                               int head_dim) {
   if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
-  return dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2);
+  return dsa::slice_region(n_heads, head_dim, static_cast<int64_t>(rows)).bytes +
+         dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2);
 }
 
 extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
@@ -119,8 +182,9 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return DSA_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  void* q = ws;
-  void* w = ws + dsa::align256(static_cast<size_t>(rows) * n_heads * head_dim * 2);
+  const size_t wreg = dsa::slice_region(n_heads, head_dim, rows).bytes;
+  void* q = ws + wreg;
+  void* w = ws + wreg + dsa::align256(static_cast<size_t>(rows) * n_heads * head_dim * 2);
   int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
                             rope_dim, seqlen);
   if (st != DSA_OK) return st;
@@ -130,8 +194,8 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
                         n_cand, topk, start_pos, ratio);
   if (st != DSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = dsa::launch_qproj_rope(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, rope_dim,
-                              seqlen, s);
+  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
+                      rope_dim, seqlen, ws, s);
   if (st != DSA_OK) return st;
   st = dsa::launch_wproj(x, w_proj, w, rows, dim, w_scale, s);
   if (st != DSA_OK) return st;

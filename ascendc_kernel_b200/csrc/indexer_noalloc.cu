@@ -3,8 +3,8 @@
 // Some callers cannot hand this library a workspace: plug-ins whose host
 // framework owns all device memory and forbids allocating inside an operator,
 // and latency-critical paths where a cudaMalloc/cudaFree (which can
-// synchronize the device) is not acceptable. For them the q and w
-// intermediates of the indexer live in a fixed array compiled into this
+// synchronize the device) is not acceptable. For them the operand slices and
+// the q and w intermediates of the indexer live in a fixed array compiled into this
 // library, of kNoAllocScratchBytes per device; every device that loads the
 // library keeps it until the process exits.
 //
@@ -22,7 +22,7 @@
 namespace dsa {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t{48} << 20;  // 48 MiB
+constexpr size_t kNoAllocScratchBytes = size_t{64} << 20;  // 64 MiB
 
 static __device__ __align__(256) unsigned char g_indexer_scratch[kNoAllocScratchBytes];
 

@@ -208,11 +208,13 @@ def qproj_rope(qr: torch.Tensor, wq: torch.Tensor, cos: torch.Tensor, sin: torch
     qr = qr.contiguous()
     rows = qr.numel() // qr.shape[-1]
     out = torch.empty(rows, n_heads * head_dim, dtype=torch.bfloat16, device=qr.device)
+    nbytes = lib().dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=qr.device)
     stream = torch.cuda.current_stream(qr.device).cuda_stream
     with torch.cuda.device(qr.device):
         call("dsa_indexer_qproj_rope", qr.data_ptr(), wq.contiguous().data_ptr(),
              cos.contiguous().data_ptr(), sin.contiguous().data_ptr(), out.data_ptr(), rows,
-             qr.shape[-1], n_heads, head_dim, rope_dim, seqlen, stream)
+             qr.shape[-1], n_heads, head_dim, rope_dim, seqlen, ws.data_ptr(), nbytes, stream)
     return out
 
 

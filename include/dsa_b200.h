@@ -102,8 +102,10 @@ int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx, int idx_
  *     qr [rows, q_lora_rank] bf16, wq_b [n_heads*head_dim, q_lora_rank] bf16,
  *     cos/sin [seqlen, rope_dim/2] fp32 (position of row r is r % seqlen),
  *     q_out [rows, n_heads*head_dim] bf16.
- *     Supported: head_dim == 64, q_lora_rank a multiple of 64 and <= 256,
- *     rope_dim even and <= head_dim.
+ *     Supported: n_heads <= 16, head_dim == 64, q_lora_rank a multiple of 64 and <= 256,
+ *     rope_dim even and <= head_dim. workspace (256-byte aligned) receives the
+ *     int8 slices of wq_b and qr that the call builds;
+ *     dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim) bytes are enough.
  *     Replaces the aclnnMatmul executor (src/task2_indexer.py:763-809) plus
  *     launch_ix_rope / run_rope (src/indexer_kernel_aiv.asc:110-111,
  *     src/task2_indexer.py:724-728); semantics reference/task2_v0_ref.py:129-131.
@@ -111,7 +113,7 @@ int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx, int idx_
 int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_tab,
                            const float* sin_tab, void* q_out, int64_t rows, int q_lora_rank,
                            int n_heads, int head_dim, int rope_dim, int64_t seqlen,
-                           void* stream);
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* (b) w = bf16(bf16(x . w_proj^T) * scale).  x [rows, dim] bf16,
  *     w_proj [n_heads, dim] bf16, w_out [rows, n_heads] bf16.
@@ -159,11 +161,11 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
  * time -- plug-ins whose host framework owns all device memory and forbids
  * allocating inside an operator, or latency-critical paths where a
  * cudaMalloc/cudaFree (which can synchronize the device) is not acceptable.
- * Same arguments and result as dsa_indexer_fwd, without the workspace: the q
- * and w intermediates live in a fixed 48 MiB array inside the library, one per
+ * Same arguments and result as dsa_indexer_fwd, without the workspace: the
+ * operand slices and the q and w intermediates live in a fixed 64 MiB array inside the library, one per
  * device that loads it, held until the process exits. The request needs
- * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) <= 48 MiB,
- * i.e. at most 24,197 tokens (batch*seqlen) at 16 heads x 64 dims; larger
+ * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) <= 64 MiB,
+ * i.e. at most 23,219 tokens (batch*seqlen) at 16 heads x 64 dims; larger
  * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
  * device looks up the array's address; make it before any stream capture.
  * Every call on a device uses the same array, so calls that overlap on the GPU

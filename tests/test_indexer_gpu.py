@@ -56,6 +56,42 @@ def _model_from_golden(g, c, p, dev):
     return m
 
 
+def _edge_rows(mode, rows, k, gen):
+    x = torch.randn(rows, k, generator=gen)
+    if mode == "wide":  # exponents spread over 2^-24..2^4 inside every row
+        x = x * torch.exp2(torch.randint(-24, 5, (rows, k), generator=gen).float())
+    elif mode == "special":
+        x[0] = 0.0                                   # all-zero row
+        x[1] = x[1] * 1e-39                          # subnormal bf16 row
+        x[2, : k // 2] = 1e-39                       # subnormals beside normals
+        x[3] = torch.where(torch.arange(k) % 2 == 0, 1.0, -1.0)  # cancels against row 6
+        x[4] = x[4] * 1e30                           # overflows against itself
+        x[6] = 2.0
+        x[5, 1:] = 0.0                               # a single nonzero
+    return x.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("k", [64, 192, 256])
+@pytest.mark.parametrize("mode", ["normal", "wide", "special"])
+def test_qproj_slicing_edge_cases(cuda_device, k, mode):
+    """q projection on operands that stress the int8 slicing: q_lora_rank that
+    is not a multiple of the 128-wide slice box, exponent ranges wider than the
+    three slices (remainders, fp64 fallbacks), zero / subnormal / huge rows."""
+    gen = torch.Generator().manual_seed(k * 7 + len(mode))
+    rows, seqlen, n_heads, rd = 300, 150, 16, 32
+    qr = _edge_rows(mode, rows, k, gen)
+    wq = _edge_rows(mode, n_heads * 64, k, gen)
+    cos = torch.rand(seqlen, rd // 2, generator=gen)
+    sin = torch.rand(seqlen, rd // 2, generator=gen)
+    dev = cuda_device
+    q = ix.qproj_rope(qr.to(dev), wq.to(dev), cos.to(dev), sin.to(dev), n_heads, 64, rd, seqlen)
+    want = oracle.rope(oracle.linear_bf16(to_u16(qr), to_u16(wq)), cos.numpy(), sin.numpy(),
+                       n_heads, 64, rd, seqlen)
+    got = to_u16(q)
+    assert np.array_equal(got, want), int((got != want).sum())
+    assert _native.device_error(dev.index) == 0
+
+
 @pytest.mark.parametrize("p", ["p_", "d_"])
 def test_forward_golden_equals_oracle(golden_dir, cuda_device, p):
     g, c = golden(golden_dir, p)

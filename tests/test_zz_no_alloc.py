@@ -3,7 +3,7 @@
 It serves callers that cannot allocate device memory when they call the
 indexer -- e.g. a plug-in whose host framework owns all device memory, or a
 latency-critical path that must not pay for cudaMalloc/cudaFree -- by keeping
-the q and w intermediates in a fixed 48 MiB array inside the library. These
+the q and w intermediates in a fixed 64 MiB array inside the library. These
 tests call it through the C ABI and check that two calls in a row (different
 inputs, same shared array) return exactly the indices of the workspace-taking
 entry point, dsa_indexer_fwd, and that an oversized request is rejected.
@@ -22,7 +22,20 @@ from ascendc_kernel_b200 import indexer as ix
 pytestmark = pytest.mark.gpu
 
 DSA_ERR_WORKSPACE = 5
-MAX_TOKENS = 24197  # 48 MiB / (16 heads * 64 dims * 2 B + 16 * 2 B), 256-byte aligned parts
+LIMIT_BYTES = 64 << 20  # the fixed in-library array
+
+
+def _max_tokens():
+    """Largest batch*seqlen whose workspace fits the fixed array (16 heads x 64)."""
+    lib = _native.lib()
+    lo, hi = 1, 1 << 20
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if lib.dsa_indexer_workspace_bytes(1, mid, 16, 64) <= LIMIT_BYTES:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
 
 
 def _inputs(seed, dev, batch=8, seqlen=2600):
@@ -99,5 +112,5 @@ def test_no_alloc_rejects_requests_beyond_its_array(cuda_device):
     head, _ = _common_args(d, out)
     stream = torch.cuda.current_stream(dev).cuda_stream
     tail = _tail(d, stream)
-    tail[0], tail[1] = 1, MAX_TOKENS + 1   # batch, seqlen beyond the fixed array
+    tail[0], tail[1] = 1, _max_tokens() + 1   # batch, seqlen beyond the fixed array
     assert lib.dsa_indexer_fwd_noalloc(*head, *tail) == DSA_ERR_WORKSPACE
