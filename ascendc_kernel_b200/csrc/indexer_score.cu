@@ -50,7 +50,7 @@ constexpr int kOffKeys = kOffKV + kKVStages * kKVBytes;       // 114688
 constexpr int kOffQN = kOffKeys + kTB * kMaxT * 4;            // 180224
 constexpr int kOffW = kOffQN + kQRows * 4;                    // 181248
 constexpr int kOffSel = kOffW + kQRows * 4;                   // 182272: per warp hist + sel
-constexpr int kHistCopies = 4;                                // lanes spread over copies
+constexpr int kHistCopies = 4;                                // histogram + drain queue space
 constexpr int kSelBytes = kHistCopies * 256 * 4 + kMaxK * 4;  // 5 KB per warp
 constexpr int kOffNV = kOffSel + 8 * kSelBytes;               // 223232: [16] int
 constexpr int kOffWP = kOffNV + kTB * 4;                      // [256] w as bf16x2 {w, w}
@@ -107,29 +107,6 @@ __device__ __forceinline__ float row_norm64(const uint8_t* base, int row) {
   return norm_upper(ss, kDim);
 }
 
-// Exact dot product of q row `qrow` and kv row `krow` (both SW128 in smem):
-// exact fp64 products summed in ascending dimension order (the oracle's
-// order), rounded once to bf16.
-__device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qrow,
-                                                   const uint8_t* kvbase, int krow) {
-  double acc = 0.0;
-#pragma unroll
-  for (int ch = 0; ch < 8; ++ch) {
-    const uint4 a = *reinterpret_cast<const uint4*>(qbase + sw128_off(qrow, ch));
-    const uint4 b = *reinterpret_cast<const uint4*>(kvbase + sw128_off(krow, ch));
-    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      acc = fma(static_cast<double>(bf16lo_to_f32(aw[e])), static_cast<double>(bf16lo_to_f32(bw[e])),
-                acc);
-      acc = fma(static_cast<double>(bf16hi_to_f32(aw[e])), static_cast<double>(bf16hi_to_f32(bw[e])),
-                acc);
-    }
-  }
-  return round_f64_to_bf16(acc);
-}
-
 // score key of candidate k from its 16 correctly rounded bf16 head scores:
 // e_h = bf16(relu(s_h) * w_h), score = bf16(sum_h e_h) (pairwise fp64; the 16
 // terms have 8 significant bits, so the sum is exact like the oracle's),
@@ -163,45 +140,74 @@ __device__ __forceinline__ void load_token_vectors(const float* qn, const float*
   }
 }
 
-// Per-warp queue of (token, kv row) pairs whose score could not be certified.
-// Entry: word 0 = token slot << 16 | kv row in the chunk, word 1 = mask of the
-// heads whose bf16 score is uncertain, words 2..9 = the 16 head scores as bf16
-// pairs (exact for the heads not in the mask).
-constexpr int kRqWords = 10;
+// Exact dot product of q row `qrow` and kv row `krow` (both SW128 in smem):
+// exact fp64 products summed in ascending dimension order (the oracle's
+// order), rounded once to bf16.
+__device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qrow,
+                                                   const uint8_t* kvbase, int krow) {
+  double acc = 0.0;
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint4 a = *reinterpret_cast<const uint4*>(qbase + sw128_off(qrow, ch));
+    const uint4 b = *reinterpret_cast<const uint4*>(kvbase + sw128_off(krow, ch));
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc = fma(static_cast<double>(bf16lo_to_f32(aw[e])), static_cast<double>(bf16lo_to_f32(bw[e])),
+                acc);
+      acc = fma(static_cast<double>(bf16hi_to_f32(aw[e])), static_cast<double>(bf16hi_to_f32(bw[e])),
+                acc);
+    }
+  }
+  return round_f64_to_bf16(acc);
+}
 
-// One lane per queued pair: exact recomputation of the uncertain heads, then
-// the exact score chain; writes the key.
+// Per-warp queue of (token, kv row) pairs of the current chunk whose score
+// could not be certified. Entry: word 0 = token slot << 16 | kv row of the
+// chunk, words 1..16 = per head the bf16 pair {RNE(v+E), RNE(v-E)} of
+// the interval that holds the head's exact bf16 score.
+constexpr int kRqWords = 17;
+
+__device__ __forceinline__ bool bf16_positive(uint32_t h16) {
+  return h16 != 0u && !(h16 & 0x8000u);
+}
+
+// One lane per queued pair: exact recomputation of the heads whose interval is
+// open and can be positive, then the exact score chain; writes the key.
 __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
-                                         const uint8_t* kvs, const float* wv, uint32_t* keys,
-                                         int chunk_base, int lane) {
+                                         const uint8_t* kvs, int chunk_base, const float* wv,
+                                         uint32_t* keys, int lane) {
   __syncwarp();
   for (int i = lane; i < n; i += 32) {
     uint32_t* e = rq + i * kRqWords;
     const int tt = static_cast<int>(e[0] >> 16);
     const int row = static_cast<int>(e[0] & 0xFFFFu);
-    uint32_t m = e[1];
+    const int k = chunk_base + row;
+    uint32_t open = 0;  // heads whose interval is open and can be positive
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      const uint32_t pr = e[1 + h];
+      const uint32_t lo16 = pr & 0xFFFFu, hi16 = pr >> 16;
+      if (lo16 != hi16 && bf16_positive(hi16)) open |= 1u << h;
+    }
+    // one rolled loop (a single copy of the exact dot in the code); the exact
+    // value replaces the interval in the entry
 #pragma unroll 1
-    while (m) {
-      const int h = __ffs(static_cast<int>(m)) - 1;
-      m &= m - 1;
-      const uint32_t bits = exact_dot_bits(qs, tt * 16 + h, kvs, row);
-      const uint32_t w2 = e[2 + (h >> 1)];
-      e[2 + (h >> 1)] = (h & 1) ? ((w2 & 0xFFFFu) | (bits << 16)) : ((w2 & 0xFFFF0000u) | bits);
+    while (open) {
+      const int h = __ffs(static_cast<int>(open)) - 1;
+      open &= open - 1;
+      e[1 + h] = exact_dot_bits(qs, tt * 16 + h, kvs, row);
     }
     uint32_t sb[16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t w2 = e[2 + j];
-      sb[2 * j] = w2 & 0xFFFFu;
-      sb[2 * j + 1] = w2 >> 16;
-    }
+    for (int h = 0; h < 16; ++h) sb[h] = e[1 + h] & 0xFFFFu;  // certified, exact, or relu'd to 0
     float wf[16];
 #pragma unroll
     for (int h4 = 0; h4 < 4; ++h4) {
       const float4 c = reinterpret_cast<const float4*>(wv + tt * 16)[h4];
       wf[4 * h4 + 0] = c.x; wf[4 * h4 + 1] = c.y; wf[4 * h4 + 2] = c.z; wf[4 * h4 + 3] = c.w;
     }
-    const int k = chunk_base + row;
     keys[tt * kMaxT + k] = score_key(sb, wf, k);
   }
   __syncwarp();
@@ -265,79 +271,55 @@ __device__ __forceinline__ void sort_and_store(const uint32_t* sel, int nsel, in
   }
 }
 
-// Top-Ksel of the n unique keys in `keys` (smem) by one warp: 8-bit radix
-// select of the Ksel-th largest key, compaction of the keys >= it, sort.
-__device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* hist, uint32_t* sel,
-                          int64_t* out_row, int64_t offset, int lane) {
+// Top-Ksel of the n keys in `keys` (smem, in candidate order) by one warp. A
+// key is (orderable score << 16) | (0xFFFF - k), so the order is score
+// descending, then k ascending. The keys are held in registers (key r*32+lane
+// in v[r]); a binary search over the 16 score bits finds the largest score thr
+// with at least Ksel keys scoring >= thr, and keys scoring exactly thr are
+// taken in k order (the order they are stored in) up to Ksel. The selected keys
+// are then compacted and sorted.
+template <int R>
+__device__ __forceinline__ void warp_topk_r(const uint32_t* keys, int n, int K_out, uint32_t* sel,
+                                            int64_t* out_row, int64_t offset, int lane) {
   const int ksel = n < K_out ? n : K_out;
-  uint32_t thr = 0;  // keys >= thr are selected
-  if (n > ksel) {
-    uint32_t prefix = 0, pmask = 0;
-    int need = ksel;
-    // The leading key bits (sign and exponent of similar scores) take few
-    // values, so lanes spread their atomics over kHistCopies histograms.
-    uint32_t* my_hist = hist + (lane & (kHistCopies - 1)) * 256;
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  uint32_t v[R];
 #pragma unroll
-      for (int j = 0; j < 8 * kHistCopies; ++j) hist[lane * 8 * kHistCopies + j] = 0;
-      __syncwarp();
-      for (int i = lane; i < n; i += 32) {
-        const uint32_t k = keys[i];
-        if ((k & pmask) == prefix) atomicAdd(&my_hist[(k >> shift) & 0xFFu], 1u);
-      }
-      __syncwarp();
-      // lane l owns bins 255-8l .. 248-8l (descending digit order)
-      uint32_t c[8];
-      uint32_t tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int bin = 255 - lane * 8 - j;
-        c[j] = 0;
-#pragma unroll
-        for (int cp = 0; cp < kHistCopies; ++cp) c[j] += hist[cp * 256 + bin];
-        tot += c[j];
-      }
-      uint32_t incl = tot;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += x;
-      }
-      const uint32_t excl = incl - tot;  // keys with a larger digit than my bins
-      // the lane whose range contains the crossing point finds the digit
-      int digit = -1;
-      uint32_t above = 0;
-      if (excl < static_cast<uint32_t>(need) && incl >= static_cast<uint32_t>(need)) {
-        uint32_t run = excl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (digit < 0 && run + c[j] >= static_cast<uint32_t>(need)) {
-            digit = 255 - lane * 8 - j;
-            above = run;
-          }
-          run += c[j];
-        }
-      }
-      const uint32_t ball = __ballot_sync(0xFFFFFFFFu, digit >= 0);
-      const int src = __ffs(static_cast<int>(ball)) - 1;
-      digit = __shfl_sync(0xFFFFFFFFu, digit, src);
-      above = __shfl_sync(0xFFFFFFFFu, above, src);
-      need -= static_cast<int>(above);
-      prefix |= static_cast<uint32_t>(digit) << shift;
-      pmask |= 0xFFu << shift;
-      __syncwarp();
-    }
-    thr = prefix;
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < n ? keys[i] : 0u;  // a real key scores >= 1, padding scores 0
   }
-  // compact the selected keys (exactly ksel of them: keys are unique)
-  int base = 0;
-  for (int i0 = 0; i0 < n; i0 += 32) {
-    const int i = i0 + lane;
-    const uint32_t k = i < n ? keys[i] : 0u;
-    const bool take = i < n && k >= thr;
+  const bool take_all = n <= ksel;
+  uint32_t thr = 0;
+  int need_ties = 0;
+  if (!take_all) {
+    for (int bit = 15; bit >= 0; --bit) {
+      const uint32_t cand = (thr | (1u << bit)) << 16;
+      int c = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) c += v[r] >= cand ? 1 : 0;
+      c = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
+      if (c >= ksel) thr |= 1u << bit;
+    }
+    const uint32_t above = (thr + 1) << 16;
+    int c = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) c += v[r] >= above ? 1 : 0;
+    need_ties = ksel - static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
+  }
+  int base = 0, ties = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const uint32_t k = v[r];
+    const uint32_t sc = k >> 16;
+    const bool valid = r * 32 + lane < n;
+    const bool tie = !take_all && valid && sc == thr;
+    const uint32_t tb = __ballot_sync(0xFFFFFFFFu, tie);
+    const bool take =
+        valid && (take_all || sc > thr || (tie && ties + __popc(tb & lt_mask) < need_ties));
+    ties += __popc(tb);
     const uint32_t b = __ballot_sync(0xFFFFFFFFu, take);
-    if (take) sel[base + __popc(b & ((1u << lane) - 1u))] = k;
+    if (take) sel[base + __popc(b & lt_mask)] = k;
     base += __popc(b);
   }
   __syncwarp();
@@ -346,6 +328,16 @@ __device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* hist
   else
     sort_and_store<8>(sel, base, K_out, out_row, offset, lane);
   __syncwarp();
+}
+
+__device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* sel, int64_t* out_row,
+                          int64_t offset, int lane) {
+  if (n <= 256)
+    warp_topk_r<8>(keys, n, K_out, sel, out_row, offset, lane);
+  else if (n <= 512)
+    warp_topk_r<16>(keys, n, K_out, sel, out_row, offset, lane);
+  else
+    warp_topk_r<32>(keys, n, K_out, sel, out_row, offset, lane);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -519,6 +511,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Early exits below always fall through to the CTA-wide barrier 3, which
       // both warpgroups reach the same number of times.
       ok = named_bar_and(1 + wg, 128, ok);
+      // the selection scratch of this warp is idle until the selection: it holds
+      // the queue of pairs that need an exact recomputation
+      uint32_t* rq = hist;
+      constexpr int kRqCap = kSelBytes / 4 / kRqWords;
       for (int c = 0; ok && c < nch; ++c, ++gc) {
         const int s = gc % kKVStages;
         const int ab = gc & 1;
@@ -532,13 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
           tc_fence_after();
           const float kvn = row_norm64(kvs, row) * kGamma;
-          // the selection scratch of this warp is idle during the chunk phase:
-          // it holds the queue of pairs that need an exact recomputation
-          uint32_t* rq = hist;
-          constexpr int kRqCap = kSelBytes / 4 / kRqWords;
+          int rq_n = 0;
           const uint32_t* wpk = reinterpret_cast<const uint32_t*>(smem + kOffWP);
           const uint32_t* psel = reinterpret_cast<const uint32_t*>(smem + kOffPS);
-          int rq_n = 0;
 #pragma unroll 1
           for (int tl = 0; tl < 8; tl += 2) {
             // two tokens per TMEM load: 32 columns = 2 tokens x 16 heads
@@ -554,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // monotone) and the head sum (fp32, rounded outward). If both ends
               // of the sum round to the same bf16, that is the exact score.
               float slo[4] = {0.f, 0.f, 0.f, 0.f}, shi[4] = {0.f, 0.f, 0.f, 0.f};
-              uint32_t unc = 0, lob[8];
+              uint32_t prs[16];
 #pragma unroll
               for (int h4 = 0; h4 < 4; ++h4) {
                 const float4 qv4 = reinterpret_cast<const float4*>(qn + tt * 16)[h4];
@@ -572,11 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
                       : "=r"(pr)
                       : "f"(__fadd_ru(v, E)), "f"(__fsub_rd(v, E)));
-                  const uint32_t lo16 = pr & 0xFFFFu, hi16 = pr >> 16;
-                  // uncertain: the ends differ and the upper end is positive
-                  const bool hipos = hi16 != 0u && !(hi16 & 0x8000u);
-                  unc |= (lo16 != hi16 && hipos) ? (1u << h) : 0u;
-                  if (h & 1) lob[h >> 1] |= lo16 << 16; else lob[h >> 1] = lo16;
+                  prs[h] = pr;
                   uint32_t e2 = __byte_perm(pr, 0, psa[i]);
                   asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
                   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
@@ -595,15 +583,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {
-                  drain_queue(rq, rq_n, qs, kvs, wv, keys, c * kChunk, lane);
+                  drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, lane);
                   rq_n = 0;
                 }
                 if (need) {
                   uint32_t* e = rq + (rq_n + __popc(bal & ((1u << lane) - 1u))) * kRqWords;
                   e[0] = (static_cast<uint32_t>(tt) << 16) | static_cast<uint32_t>(row);
-                  e[1] = unc;
 #pragma unroll
-                  for (int q2 = 0; q2 < 8; ++q2) e[2 + q2] = lob[q2];
+                  for (int h = 0; h < 16; ++h) e[1 + h] = prs[h];
                 }
                 rq_n += __popc(bal);
               }
@@ -613,7 +600,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (rq_n > 0) drain_queue(rq, rq_n, qs, kvs, wv, keys, c * kChunk, lane);
+          if (__any_sync(0xFFFFFFFFu, rq_n > 0))
+            drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, lane);
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
         }
@@ -628,8 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tok >= p.S) continue;
         const int64_t nv = n_valid(p, tok);
         int64_t* out_row = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
-        warp_topk(keys + tt * kMaxT, static_cast<int>(nv), p.K, hist, sel, out_row, p.offset,
-                  lane);
+        warp_topk(keys + tt * kMaxT, static_cast<int>(nv), p.K, sel, out_row, p.offset, lane);
       }
       if (!named_bar_and(3, 256, ok)) break;
     }
