@@ -15,8 +15,12 @@ int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* si
 int launch_wproj(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
                  cudaStream_t stream);
 int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
-                      int64_t* out, int64_t batch, int64_t seqlen, int64_t n_cand, int topk,
-                      int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream);
+                      int64_t* out, void* scores, int64_t batch, int64_t seqlen, int64_t n_cand,
+                      int topk, int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream);
+int launch_topk_sort(const void* scores, int64_t ld, int64_t* out, int64_t batch, int64_t seqlen,
+                     int64_t n_cand, int topk, int64_t start_pos, int ratio, int64_t offset,
+                     cudaStream_t stream);
+int topk_sort_max_cand();
 
 namespace {
 constexpr int kHeadDim = 64;
@@ -101,6 +105,16 @@ int check_wproj(const void* x, const void* wp, const void* w_out, int64_t rows, 
   return DSA_OK;
 }
 
+// Short candidate lists are scored and selected in one kernel (keys in shared
+// memory); longer ones go through a score buffer and a sort kernel.
+bool score_fused(int64_t n_cand, int topk) { return n_cand <= kMaxCand && topk <= kMaxTopk; }
+
+size_t score_buffer_bytes(int64_t batch, int64_t seqlen, int64_t n_cand, int topk) {
+  if (batch <= 0 || seqlen <= 0 || n_cand <= 0 || score_fused(n_cand, topk)) return 0;
+  return align256(static_cast<size_t>(batch) * static_cast<size_t>(seqlen) *
+                  static_cast<size_t>(n_cand) * 2);
+}
+
 int check_score(const void* q, const void* w, const void* kv, int64_t kv_bstride,
                 const int64_t* out, int64_t batch, int64_t seqlen, int n_heads, int head_dim,
                 int64_t n_cand, int topk, int64_t start_pos, int ratio) {
@@ -109,7 +123,7 @@ int check_score(const void* q, const void* w, const void* kv, int64_t kv_bstride
     return DSA_ERR_INVALID_ARGUMENT;
   if (n_heads != kScoreHeads || head_dim != kHeadDim) return DSA_ERR_UNSUPPORTED;
   if (topk > n_cand) return DSA_ERR_INVALID_ARGUMENT;
-  if (n_cand > kMaxCand || topk > kMaxTopk) return DSA_ERR_UNSUPPORTED;
+  if (!score_fused(n_cand, topk) && n_cand > topk_sort_max_cand()) return DSA_ERR_UNSUPPORTED;
   if (kv_bstride < n_cand * kHeadDim || kv_bstride % kHeadDim != 0) return DSA_ERR_INVALID_ARGUMENT;
   if (batch * seqlen * kScoreHeads > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
   if ((batch - 1) * (kv_bstride / kHeadDim) + n_cand > kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
@@ -143,24 +157,52 @@ extern "C" int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out,
   return dsa::launch_wproj(x, w_proj, w_out, rows, dim, scale, static_cast<cudaStream_t>(stream));
 }
 
+namespace dsa {
+namespace {
+// Scores, then (long lists) the sort; `scores` is the score buffer or null.
+int run_score(const void* q, const void* w, const void* kv, int64_t kv_bstride, int64_t* out,
+              void* scores, int64_t batch, int64_t seqlen, int64_t n_cand, int topk,
+              int64_t start_pos, int ratio, int64_t offset, cudaStream_t s) {
+  if (score_fused(n_cand, topk))
+    return launch_score_topk(q, w, kv, kv_bstride, out, nullptr, batch, seqlen, n_cand, topk,
+                             start_pos, ratio, offset, s);
+  int st = launch_score_topk(q, w, kv, kv_bstride, out, scores, batch, seqlen, n_cand, topk,
+                             start_pos, ratio, offset, s);
+  if (st != DSA_OK) return st;
+  return launch_topk_sort(scores, n_cand, out, batch, seqlen, n_cand, topk, start_pos, ratio,
+                          offset, s);
+}
+}  // namespace
+}  // namespace dsa
+
+extern "C" size_t dsa_indexer_score_workspace_bytes(int64_t batch, int64_t seqlen, int64_t n_cand,
+                                                    int topk) {
+  return dsa::score_buffer_bytes(batch, seqlen, n_cand, topk);
+}
+
 extern "C" int dsa_indexer_score_topk(const void* q, const void* w, const void* kv_cache,
                                       int64_t kv_batch_stride, int64_t* out, int64_t batch,
                                       int64_t seqlen, int n_heads, int head_dim, int64_t n_cand,
                                       int topk, int64_t start_pos, int ratio, int64_t offset,
-                                      void* stream) {
+                                      void* workspace, size_t workspace_bytes, void* stream) {
   int st = dsa::check_score(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_heads,
                             head_dim, n_cand, topk, start_pos, ratio);
   if (st != DSA_OK || batch == 0 || seqlen == 0 || topk == 0) return st;
-  return dsa::launch_score_topk(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_cand, topk,
-                                start_pos, ratio, offset, static_cast<cudaStream_t>(stream));
+  const size_t need = dsa::score_buffer_bytes(batch, seqlen, n_cand, topk);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need ||
+                   (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
+    return DSA_ERR_WORKSPACE;
+  return dsa::run_score(q, w, kv_cache, kv_batch_stride, out, workspace, batch, seqlen, n_cand,
+                        topk, start_pos, ratio, offset, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads,
-                                              int head_dim) {
+                                              int head_dim, int64_t n_cand, int topk) {
   if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
   return dsa::slice_region(n_heads, head_dim, static_cast<int64_t>(rows)).bytes +
-         dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2);
+         dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2) +
+         dsa::score_buffer_bytes(batch, seqlen, n_cand, topk);
 }
 
 extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
@@ -177,7 +219,8 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
   const int64_t n_cand = (start_pos + seqlen) / ratio;
   const int topk = static_cast<int>(index_topk < n_cand ? index_topk : n_cand);
   if (topk <= 0) return DSA_ERR_INVALID_ARGUMENT;
-  const size_t need = dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim);
+  const size_t need =
+      dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk);
   if (workspace == nullptr || workspace_bytes < need ||
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return DSA_ERR_WORKSPACE;
@@ -185,6 +228,7 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
   const size_t wreg = dsa::slice_region(n_heads, head_dim, rows).bytes;
   void* q = ws + wreg;
   void* w = ws + wreg + dsa::align256(static_cast<size_t>(rows) * n_heads * head_dim * 2);
+  void* scores = static_cast<uint8_t*>(w) + dsa::align256(static_cast<size_t>(rows) * n_heads * 2);
   int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
                             rope_dim, seqlen);
   if (st != DSA_OK) return st;
@@ -199,6 +243,6 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
   if (st != DSA_OK) return st;
   st = dsa::launch_wproj(x, w_proj, w, rows, dim, w_scale, s);
   if (st != DSA_OK) return st;
-  return dsa::launch_score_topk(q, w, kv_cache, kv_batch_stride, out, batch, seqlen, n_cand, topk,
-                                start_pos, ratio, offset, s);
+  return dsa::run_score(q, w, kv_cache, kv_batch_stride, out, scores, batch, seqlen, n_cand, topk,
+                        start_pos, ratio, offset, s);
 }

@@ -55,9 +55,11 @@ extern "C" int dsa_indexer_fwd_noalloc(const void* x, const void* qr, const void
                                        int head_dim, int rope_dim, int index_topk,
                                        int64_t start_pos, int ratio, int64_t offset,
                                        float w_scale, void* stream) {
-  if (batch < 0 || seqlen < 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || seqlen < 0 || ratio <= 0 || start_pos < 0) return DSA_ERR_INVALID_ARGUMENT;
   if (batch == 0 || seqlen == 0) return DSA_OK;
-  const size_t need = dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim);
+  const int64_t n_cand = (start_pos + seqlen) / ratio;
+  const int topk = static_cast<int>(index_topk < n_cand ? index_topk : n_cand);
+  const size_t need = dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk);
   if (need == 0) return DSA_ERR_INVALID_ARGUMENT;
   if (need > dsa::kNoAllocScratchBytes) return DSA_ERR_WORKSPACE;
   void* ws = nullptr;

@@ -65,7 +65,6 @@ __host__ __device__ constexpr float gamma_for(int nchunks) {
 // apart, so one MMA of A_i against the stacked B (N = 192) adds A_i.B1,
 // A_i.B2, A_i.B3 into levels i+1, i+2, i+3 at once: three MMAs per 32-wide k
 // step instead of eight.
-constexpr int kSigmaNonFinite = 1 << 20;  // as written by indexer_split.cu
 constexpr int kQBN = 64;                  // one head per tile
 constexpr int kQMaxK = 256;
 constexpr int kQGroup = 4;                // tiles (heads) per unit

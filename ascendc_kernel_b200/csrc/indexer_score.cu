@@ -76,7 +76,9 @@ struct Params {
   int units;
   int64_t kv_rows_per_batch;  // kv_batch_stride / 64
   const uint16_t* w;  // [B*S, 16]
-  int64_t* out;       // [B*S, K]
+  int64_t* out;       // [B*S, K] (top-k in the kernel), or
+  uint16_t* scores;   // [B*S, score_ld] bf16 scores of the valid candidates (sorted later)
+  int64_t score_ld;
   unsigned int* err;
 };
 
@@ -173,11 +175,17 @@ __device__ __forceinline__ bool bf16_positive(uint32_t h16) {
   return h16 != 0u && !(h16 & 0x8000u);
 }
 
+// bf16 bits of a score from its orderable image.
+__device__ __forceinline__ uint32_t ord_to_bf16(uint32_t ord) {
+  return (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+}
+
 // One lane per queued pair: exact recomputation of the heads whose interval is
-// open and can be positive, then the exact score chain; writes the key.
+// open and can be positive, then the exact score chain; writes the key (or,
+// with gs, the bf16 score to gs[token slot * gld + k]).
 __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
                                          const uint8_t* kvs, int chunk_base, const float* wv,
-                                         uint32_t* keys, int lane) {
+                                         uint32_t* keys, uint16_t* gs, int64_t gld, int lane) {
   __syncwarp();
   for (int i = lane; i < n; i += 32) {
     uint32_t* e = rq + i * kRqWords;
@@ -208,7 +216,11 @@ __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
       const float4 c = reinterpret_cast<const float4*>(wv + tt * 16)[h4];
       wf[4 * h4 + 0] = c.x; wf[4 * h4 + 1] = c.y; wf[4 * h4 + 2] = c.z; wf[4 * h4 + 3] = c.w;
     }
-    keys[tt * kMaxT + k] = score_key(sb, wf, k);
+    const uint32_t key = score_key(sb, wf, k);
+    if (gs)
+      gs[tt * gld + k] = static_cast<uint16_t>(ord_to_bf16(key >> 16));
+    else
+      keys[tt * kMaxT + k] = key;
   }
   __syncwarp();
 }
@@ -489,6 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nch = unit_chunks(t0);
       const int qb = lu & 1;
       const uint8_t* qs = smem + kOffQ + qb * kQBytes;
+      uint16_t* gs = p.scores ? p.scores + (static_cast<int64_t>(b) * p.S + t0) * p.score_ld
+                              : nullptr;
       // (t,h) row of this thread for norms / weights: token 8wg + t_in/16, head t_in%16
       const int qrow = wg * 128 + t_in;
       int* nvs = reinterpret_cast<int*>(smem + kOffNV);
@@ -583,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {
-                  drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, lane);
+                  drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, gs, p.score_ld, lane);
                   rq_n = 0;
                 }
                 if (need) {
@@ -595,13 +609,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 rq_n += __popc(bal);
               }
               if (active && !need) {
-                const uint32_t ord = (tlo & 0x8000u) ? (~tlo & 0xFFFFu) : (tlo | 0x8000u);
-                keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+                if (gs) {
+                  gs[tt * p.score_ld + k] = static_cast<uint16_t>(tlo);
+                } else {
+                  const uint32_t ord = (tlo & 0x8000u) ? (~tlo & 0xFFFFu) : (tlo | 0x8000u);
+                  keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+                }
               }
             }
           }
           if (__any_sync(0xFFFFFFFFu, rq_n > 0))
-            drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, lane);
+            drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, gs, p.score_ld, lane);
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
         }
@@ -609,6 +627,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && t_in == 0) mbar_arrive(&kv_empty[s]);
       }
       if (ok && t_in == 0) mbar_arrive(&q_empty[qb]);
+      if (gs) {  // scores go to global memory; the top-k runs in its own kernel
+        if (!ok) break;
+        continue;
+      }
       // all keys of the unit are written
       if (!named_bar_and(3, 256, ok)) break;
       for (int tt = ew * 2; tt < ew * 2 + 2; ++tt) {
@@ -634,8 +656,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace ixs
 
 int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
-                      int64_t* out, int64_t batch, int64_t seqlen, int64_t n_cand, int topk,
-                      int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream) {
+                      int64_t* out, void* scores, int64_t batch, int64_t seqlen, int64_t n_cand,
+                      int topk, int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream) {
   using namespace ixs;
   DeviceInfo di;
   int st = current_device_info(&di);
@@ -676,6 +698,8 @@ int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_b
   p.kv_rows_per_batch = rows_per_batch;
   p.w = static_cast<const uint16_t*>(w);
   p.out = out;
+  p.scores = static_cast<uint16_t*>(scores);
+  p.score_ld = n_cand;
   p.err = err;
   static bool attr_done[64] = {false};
   if (!attr_done[di.device]) {

@@ -173,7 +173,7 @@ class ModelNew(nn.Module):
         assert self.n_local_heads == 16 and self.head_dim == 64, \
             "kernel specialised to index_n_heads == 16, index_head_dim == 64"
         assert self.rope_head_dim % 2 == 0 and self.rope_head_dim <= self.head_dim
-        assert T <= 1024 and K <= 256, "kernel specialised to <= 1024 candidates, top-k <= 256"
+        assert T <= 8192, "kernels support up to 8192 candidates"
         assert K >= 1, "need at least one candidate (end_pos >= compress_ratio)"
         kv = self.kv_cache
         assert kv.is_cuda and kv.dtype == torch.bfloat16 and kv.device == dev
@@ -184,7 +184,7 @@ class ModelNew(nn.Module):
         qr = qr.contiguous()
         wq, wp = self._weights_on(dev)
         cos, sin = self._rope_tables(start_pos, seqlen, dev)
-        nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim)
+        nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim, T, K)
         ws = self._workspace(nbytes, dev)
         out = torch.empty(bsz, seqlen, K, dtype=torch.int64, device=dev)
         w_scale = self.softmax_scale * self.n_heads ** -0.5
@@ -208,7 +208,7 @@ def qproj_rope(qr: torch.Tensor, wq: torch.Tensor, cos: torch.Tensor, sin: torch
     qr = qr.contiguous()
     rows = qr.numel() // qr.shape[-1]
     out = torch.empty(rows, n_heads * head_dim, dtype=torch.bfloat16, device=qr.device)
-    nbytes = lib().dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim)
+    nbytes = lib().dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim, 0, 0)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=qr.device)
     stream = torch.cuda.current_stream(qr.device).cuda_stream
     with torch.cuda.device(qr.device):
@@ -242,9 +242,11 @@ def score_topk(q: torch.Tensor, w: torch.Tensor, kv_cache: torch.Tensor, batch: 
     out = torch.empty(batch, seqlen, topk, dtype=torch.int64, device=q.device)
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
+        nbytes = lib().dsa_indexer_score_workspace_bytes(batch, seqlen, n_cand, topk)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
         call("dsa_indexer_score_topk", q.contiguous().data_ptr(), w.contiguous().data_ptr(),
              kv_cache.data_ptr(), kv_cache.stride(0), out.data_ptr(), batch, seqlen, 16, 64,
-             n_cand, topk, start_pos, ratio, offset, stream)
+             n_cand, topk, start_pos, ratio, offset, ws.data_ptr(), nbytes, stream)
     return out
 
 

@@ -105,7 +105,7 @@ int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx, int idx_
  *     Supported: n_heads <= 16, head_dim == 64, q_lora_rank a multiple of 64 and <= 256,
  *     rope_dim even and <= head_dim. workspace (256-byte aligned) receives the
  *     int8 slices of wq_b and qr that the call builds;
- *     dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim) bytes are enough.
+ *     dsa_indexer_workspace_bytes(rows, 1, n_heads, head_dim, 0, 0) bytes are enough.
  *     Replaces the aclnnMatmul executor (src/task2_indexer.py:763-809) plus
  *     launch_ix_rope / run_rope (src/indexer_kernel_aiv.asc:110-111,
  *     src/task2_indexer.py:724-728); semantics reference/task2_v0_ref.py:129-131.
@@ -131,22 +131,35 @@ int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t ro
  *     q [batch*seqlen, n_heads*head_dim] bf16, w [batch*seqlen, n_heads] bf16,
  *     kv_cache rows [k] of batch b at kv_cache + b*kv_batch_stride + k*head_dim,
  *     out [batch*seqlen, topk] int64.
- *     Supported: n_heads == 16, head_dim == 64, n_cand <= 1024, topk <= 256,
- *     topk <= n_cand; kv_batch_stride a multiple of 64 and >= n_cand*64.
+ *     Supported: n_heads == 16, head_dim == 64, topk <= n_cand <= 8192;
+ *     kv_batch_stride a multiple of 64 and >= n_cand*64. Beyond 1024 candidates
+ *     or top-256 the call needs dsa_indexer_score_workspace_bytes of workspace.
  *     Replaces launch_ix_fused / run_fused_t2 (src/indexer_kernel_mm.asc:434-436,
  *     src/task2_indexer.py:730-738); semantics reference/task2_v0_ref.py:133-144.
  */
 int dsa_indexer_score_topk(const void* q, const void* w, const void* kv_cache,
                            int64_t kv_batch_stride, int64_t* out, int64_t batch, int64_t seqlen,
                            int n_heads, int head_dim, int64_t n_cand, int topk, int64_t start_pos,
-                           int ratio, int64_t offset, void* stream);
+                           int ratio, int64_t offset, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
-/* Scratch bytes dsa_indexer_fwd needs for its q and w intermediates. */
-size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim);
+/* Score-buffer bytes dsa_indexer_score_topk needs (256-byte aligned workspace):
+ * 0 when n_cand <= 1024 and topk <= 256 (scores and selection in one kernel),
+ * else batch * seqlen * n_cand bf16 scores, sorted by a second kernel
+ * (n_cand <= 8192). No counterpart in the reference, whose kernels stop at
+ * 672 candidates. */
+size_t dsa_indexer_score_workspace_bytes(int64_t batch, int64_t seqlen, int64_t n_cand, int topk);
+
+/* Scratch bytes dsa_indexer_fwd needs: operand slices, the q and w
+ * intermediates and the score buffer of dsa_indexer_score_workspace_bytes.
+ * n_cand and topk as dsa_indexer_fwd derives them (0, 0 for the projections
+ * alone). */
+size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim,
+                                   int64_t n_cand, int topk);
 
 /* (a)+(b)+(c) in one call on one stream. workspace must hold at least
- * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) bytes, 256-byte
- * aligned. cos/sin cover positions start_pos .. start_pos+seqlen-1.
+ * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
+ * bytes, 256-byte aligned. cos/sin cover positions start_pos .. start_pos+seqlen-1.
  * n_cand = (start_pos + seqlen) / ratio; topk = min(index_topk, n_cand).
  * Replaces the whole ModelNew.forward path (src/task2_indexer.py:1056-1349),
  * semantics Model.forward in reference/task2_v0_ref.py:123-144. */
@@ -164,8 +177,9 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
  * Same arguments and result as dsa_indexer_fwd, without the workspace: the
  * operand slices and the q and w intermediates live in a fixed 64 MiB array inside the library, one per
  * device that loads it, held until the process exits. The request needs
- * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim) <= 64 MiB,
- * i.e. at most 23,219 tokens (batch*seqlen) at 16 heads x 64 dims; larger
+ * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
+ * <= 64 MiB, i.e. at most 23,219 tokens (batch*seqlen) at 16 heads x 64 dims
+ * with n_cand <= 1024 and topk <= 256 (fewer with a score buffer); larger
  * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
  * device looks up the array's address; make it before any stream capture.
  * Every call on a device uses the same array, so calls that overlap on the GPU

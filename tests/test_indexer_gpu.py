@@ -170,6 +170,43 @@ def test_heavy_ties_use_ascending_index(cuda_device):
     assert torch.equal(got, want)
 
 
+def _score_case(batch, seqlen, n_cand, topk, start_pos, offset, seed, dev, ties=False,
+                kv_rows=None):
+    """Random q, w, kv straight into the score + top-k stage, against the oracle."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(batch * seqlen, 16 * 64, generator=g).to(torch.bfloat16)
+    w = (torch.randn(batch * seqlen, 16, generator=g) * 0.25).to(torch.bfloat16)
+    kv = torch.randn(batch, kv_rows or n_cand, 64, generator=g).to(torch.bfloat16)
+    if ties:  # few distinct kv rows and integer q: many exactly equal scores
+        kv = kv[:, torch.randint(0, 5, (kv.shape[1],), generator=g)].contiguous()
+        q = q.round().to(torch.bfloat16)
+    got = ix.score_topk(q.to(dev), w.to(dev), kv.to(dev), batch, seqlen, n_cand, topk, start_pos,
+                        4, offset)
+    want, _ = oracle.index_topk(to_u16(q), to_u16(w), to_u16(kv), batch, seqlen, 16, 64, n_cand,
+                                topk, start_pos, 4, offset)
+    return got.cpu().reshape(batch * seqlen, topk), torch.from_numpy(want)
+
+
+@pytest.mark.parametrize("batch,seqlen,n_cand,topk,start_pos,offset", [
+    (1, 40, 4096, 2048, 4096 * 4 - 40, 3),   # decode over 4096 candidates, top-2048
+    (1, 4608, 1152, 512, 0, 0),              # causal prefill past 1024 candidates
+    (2, 1024, 256, 200, 0, 0),               # top-k above 256 on a short list
+    (1, 20, 8192, 1000, 8192 * 4 - 20, 0),   # the largest candidate count
+])
+def test_long_candidate_lists(cuda_device, batch, seqlen, n_cand, topk, start_pos, offset):
+    """Score buffer + radix-sort path: more than 1024 candidates or top-k above 256."""
+    got, want = _score_case(batch, seqlen, n_cand, topk, start_pos, offset, seed=n_cand + topk,
+                            dev=cuda_device)
+    assert torch.equal(got, want), int((got != want).any(-1).sum())
+    assert _native.device_error(cuda_device.index) == 0
+
+
+def test_long_candidate_lists_ties(cuda_device):
+    got, want = _score_case(1, 60, 2000, 1500, 2000 * 4 - 60, 0, seed=5, dev=cuda_device,
+                            ties=True)
+    assert torch.equal(got, want), int((got != want).any(-1).sum())
+
+
 def test_full_reference_config(cuda_device):
     """BASELINE configs[2] with the reference's seeded construction: x[8,2600,1024],
     qr[8,2600,256], kv_cache[8,650,64], top-128; indices equal to the oracle's."""

@@ -31,7 +31,7 @@ def _max_tokens():
     lo, hi = 1, 1 << 20
     while lo < hi:
         mid = (lo + hi + 1) // 2
-        if lib.dsa_indexer_workspace_bytes(1, mid, 16, 64) <= LIMIT_BYTES:
+        if lib.dsa_indexer_workspace_bytes(1, mid, 16, 64, 650, 128) <= LIMIT_BYTES:
             lo = mid
         else:
             hi = mid - 1
@@ -70,7 +70,7 @@ def _with_workspace(d, dev):
     T = d["seqlen"] // 4
     out = torch.empty(d["batch"], d["seqlen"], min(128, T), dtype=torch.int64, device=dev)
     head, _ = _common_args(d, out)
-    nbytes = lib.dsa_indexer_workspace_bytes(d["batch"], d["seqlen"], 16, 64)
+    nbytes = lib.dsa_indexer_workspace_bytes(d["batch"], d["seqlen"], 16, 64, T, min(128, T))
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
     tail = _tail(d, stream)
