@@ -6,7 +6,7 @@
 // descending, then candidate index ascending; slots past the token's valid
 // count n are -1, valid slots hold k + offset.
 //
-// One 256-thread block per token. The n scores are loaded in index order and
+// One 512-thread block per token. The n scores are loaded in index order and
 // sorted by a stable LSD radix sort over the 16-bit orderable score (two 8-bit
 // passes). Stability keeps equal scores in index order, which is exactly the
 // tie rule. Each warp owns a contiguous range of 32*J elements (lane l of step
@@ -18,9 +18,9 @@
 namespace dsa {
 namespace ixt {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxJ = 32;                  // steps of 32 per warp: n <= 8192
+constexpr int kMaxJ = 16;                  // steps of 32 per warp: n <= 8192
 constexpr int kMaxN = kWarps * 32 * kMaxJ;
 
 struct Params {
@@ -42,19 +42,24 @@ __device__ __forceinline__ uint32_t ord16(uint32_t sb) {
   return (sb & 0x8000u) ? (~sb & 0xFFFFu) : (sb | 0x8000u);
 }
 
+// J: the launch's step bound; jr <= J: steps this row needs (a warp owns
+// elements [32 jr warp, 32 jr (warp + 1))).
 template <int J>
-__device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, uint32_t* buf0,
-                                         uint32_t* buf1, uint32_t* hist, uint32_t* scan) {
+__device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, int jr,
+                                         uint32_t* buf0, uint32_t* buf1, uint32_t* hist,
+                                         uint32_t* scan) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint16_t* src = p.scores + row * p.ld;
-  const int wbase = warp * 32 * J;
+  const int wbase = warp * 32 * jr;
   uint32_t v[J];
 #pragma unroll
   for (int j = 0; j < J; ++j) {
     const int e = wbase + 32 * j + lane;  // element index = candidate k
     // padding elements carry order 0, below every real score, and sort last
-    v[j] = e < n ? (ord16(__ldg(src + e)) << 16) | (0xFFFFu - static_cast<uint32_t>(e)) : 0u;
+    v[j] = (j < jr && e < n)
+               ? (ord16(__ldg(src + e)) << 16) | (0xFFFFu - static_cast<uint32_t>(e))
+               : 0u;
   }
   uint32_t* cur = buf0;
   uint32_t* nxt = buf1;
@@ -69,6 +74,7 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, ui
     uint32_t rank[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
+      if (j >= jr) break;
       const uint32_t d = 255u - ((v[j] >> shift) & 0xFFu);  // ascending digit = descending score
       const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
       rank[j] = wh[d] + static_cast<uint32_t>(__popc(peers & lt_mask));
@@ -78,8 +84,8 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, ui
     }
     __syncthreads();
     // phase B: offset of (warp, digit) = elements of smaller digits + same digit in earlier warps
-    {
-      const int d = tid;  // kThreads == 256 digits
+    if (tid < 256) {
+      const int d = tid;  // one thread per digit
       uint32_t tot = 0;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
@@ -95,10 +101,10 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, ui
         if (lane >= o) incl += x;
       }
       if (lane == 31) scan[warp] = incl;
-      __syncthreads();
+      named_bar_sync(1, 256);
       uint32_t wpre = 0;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) wpre += w < warp ? scan[w] : 0u;
+      for (int w = 0; w < 8; ++w) wpre += w < warp ? scan[w] : 0u;
       const uint32_t base = wpre + incl - tot;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) hist[w * 256 + d] += base;
@@ -107,12 +113,16 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, ui
     // phase C: scatter
 #pragma unroll
     for (int j = 0; j < J; ++j) {
+      if (j >= jr) break;
       const uint32_t d = 255u - ((v[j] >> shift) & 0xFFu);
       nxt[wh[d] + rank[j]] = v[j];
     }
     __syncthreads();
 #pragma unroll
-    for (int j = 0; j < J; ++j) v[j] = nxt[wbase + 32 * j + lane];
+    for (int j = 0; j < J; ++j) {
+      if (j >= jr) break;
+      v[j] = nxt[wbase + 32 * j + lane];
+    }
     uint32_t* t = cur;
     cur = nxt;
     nxt = t;
@@ -127,12 +137,15 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, ui
   }
 }
 
+// J: step bound of this launch (n_cand <= kThreads * J).
+template <int J>
 __global__ void __launch_bounds__(kThreads)
     topk_sort_kernel(const Params p) {
   extern __shared__ uint32_t sm[];
   uint32_t* hist = sm;                       // [warps][256]
-  uint32_t* scan = hist + kWarps * 256;      // [warps] (padded to 32)
-  uint32_t* buf0 = scan + 32;                // [n_pad]
+  uint32_t* scan = hist + kWarps * 256;      // [8] (padded to 32)
+  uint32_t* buf0 = scan + 32;                // [kThreads * J] x 2
+  uint32_t* buf1 = buf0 + kThreads * J;
   for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
     const int64_t t = row % p.S;
     int64_t n = p.T;
@@ -140,18 +153,27 @@ __global__ void __launch_bounds__(kThreads)
       n = (t + 1) / p.ratio;
       if (n > p.T) n = p.T;
     }
-    const int J = static_cast<int>((n + kThreads - 1) / kThreads);  // steps per warp
-    const int pad = kWarps * 32 * (J > 0 ? J : 1);
-    uint32_t* buf1 = buf0 + pad;
-    const int ni = static_cast<int>(n);
-    if (J <= 1) sort_row<1>(p, row, ni, buf0, buf1, hist, scan);
-    else if (J <= 2) sort_row<2>(p, row, ni, buf0, buf1, hist, scan);
-    else if (J <= 4) sort_row<4>(p, row, ni, buf0, buf1, hist, scan);
-    else if (J <= 8) sort_row<8>(p, row, ni, buf0, buf1, hist, scan);
-    else if (J <= 16) sort_row<16>(p, row, ni, buf0, buf1, hist, scan);
-    else sort_row<32>(p, row, ni, buf0, buf1, hist, scan);
+    int jr = static_cast<int>((n + kThreads - 1) / kThreads);  // steps per warp
+    if (jr < 1) jr = 1;
+    sort_row<J>(p, row, static_cast<int>(n), jr, buf0, buf1, hist, scan);
     __syncthreads();
   }
+}
+
+template <int J>
+int launch_sort(const Params& p, const DeviceInfo& di, cudaStream_t stream) {
+  const int smem = (kWarps * 256 + 32 + 2 * kThreads * J) * 4;
+  static bool attr_done[64] = {false};
+  if (!attr_done[di.device]) {
+    const int st = cuda_status(cudaFuncSetAttribute(
+        topk_sort_kernel<J>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    if (st != DSA_OK) return st;
+    attr_done[di.device] = true;
+  }
+  int64_t grid = static_cast<int64_t>(di.num_sms) * 4;
+  if (grid > p.rows) grid = p.rows;
+  topk_sort_kernel<J><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
+  return cuda_status(cudaGetLastError());
 }
 
 }  // namespace ixt
@@ -178,24 +200,10 @@ int launch_topk_sort(const void* scores, int64_t ld, int64_t* out, int64_t batch
   p.causal = start_pos == 0 ? 1 : 0;
   p.offset = offset;
   p.rows = batch * seqlen;
-  // the J template that serves n_cand decides the buffers: 2 x warps x 32 x J keys
-  int j = 1;
-  while (kWarps * 32 * j < n_cand) j *= 2;
-  const int smem = (kWarps * 256 + 32 + 2 * kWarps * 32 * j) * 4;
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    st = cuda_status(cudaFuncSetAttribute(topk_sort_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (kWarps * 256 + 32 + 2 * kMaxN) * 4));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
-  const int64_t blocks_per_sm = (di.max_smem_optin > 0 ? 227 * 1024 : 100 * 1024) / (smem + 1024);
-  int64_t grid = di.num_sms * (blocks_per_sm > 0 ? blocks_per_sm : 1) * 2;
-  if (grid > p.rows) grid = p.rows;
-  if (grid < 1) grid = 1;
-  topk_sort_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
-  return cuda_status(cudaGetLastError());
+  if (n_cand <= kThreads * 2) return launch_sort<2>(p, di, stream);
+  if (n_cand <= kThreads * 4) return launch_sort<4>(p, di, stream);
+  if (n_cand <= kThreads * 8) return launch_sort<8>(p, di, stream);
+  return launch_sort<16>(p, di, stream);
 }
 
 }  // namespace dsa
