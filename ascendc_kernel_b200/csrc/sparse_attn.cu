@@ -449,6 +449,13 @@ int launch(const void* q, const void* kv, const void* idx, const float* sink, vo
 }  // namespace sa
 }  // namespace dsa
 
+namespace dsa {
+bool sa_long_supported(int heads, int head_dim, int nkv);
+int launch_sa_long(const void* q, const void* kv, const void* idx, int idx_elem_bytes,
+                   const float* sink, void* out, int64_t batch, int64_t m, int heads, int nkv,
+                   int topk, float scale, cudaStream_t stream);
+}  // namespace dsa
+
 extern "C" int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* idx,
                                    int idx_elem_bytes, const float* sink, void* out, int64_t batch,
                                    int64_t m, int n_heads, int head_dim, int n_kv, int topk,
@@ -459,9 +466,17 @@ extern "C" int dsa_sparse_attn_fwd(const void* q, const void* kv, const void* id
     return DSA_ERR_INVALID_ARGUMENT;
   if (idx_elem_bytes != 4 && idx_elem_bytes != 8) return DSA_ERR_INVALID_ARGUMENT;
   if (head_dim != dsa::sa::kD) return DSA_ERR_UNSUPPORTED;
+  if (n_kv > dsa::sa::kNKV || topk > 128) {
+    // long kv pool (the chained configuration): chunked kernel
+    if (!dsa::sa_long_supported(n_heads, head_dim, n_kv)) return DSA_ERR_UNSUPPORTED;
+    if (!dsa::aligned16(q) || !dsa::aligned16(kv) || !dsa::aligned16(out) ||
+        (reinterpret_cast<uintptr_t>(idx) % idx_elem_bytes) != 0)
+      return DSA_ERR_MISALIGNED;
+    if (batch == 0 || m == 0) return DSA_OK;
+    return dsa::launch_sa_long(q, kv, idx, idx_elem_bytes, sink, out, batch, m, n_heads, n_kv,
+                               topk, softmax_scale, static_cast<cudaStream_t>(stream));
+  }
   if (n_heads != 16 && n_heads != 32 && n_heads != 64 && n_heads != 128) return DSA_ERR_UNSUPPORTED;
-  if (n_kv > dsa::sa::kNKV) return DSA_ERR_UNSUPPORTED;
-  if (topk > 128) return DSA_ERR_UNSUPPORTED;
   if ((topk * idx_elem_bytes) % 16 != 0) return DSA_ERR_UNSUPPORTED;
   if ((dsa::sa::kRows / n_heads) * topk * idx_elem_bytes > dsa::sa::kIdxBytes)
     return DSA_ERR_UNSUPPORTED;

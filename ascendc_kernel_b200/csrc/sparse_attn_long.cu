@@ -1,0 +1,568 @@
+// SparseAttention forward over a long kv pool (n_kv up to 4096, any top-k), for
+// sm_100a: the chained long-context configuration, where the Lightning
+// Indexer's top-2048 of 4096 compressed kv rows feed the attention.
+//
+// Semantics (reference/task1_v0_ref.py:5-24), for every (b, t, h):
+//   s_j = q[b,t,h] . kv[b, idx_j] * scale  over the valid j (0 <= idx_j < n_kv)
+//   mx  = max(max_j s_j, sink[h])
+//   out = sum_j exp(s_j - mx) kv[b, idx_j] / (sum_j exp(s_j - mx) + exp(sink[h] - mx))
+// in the multiplicity form (c_k = #{j : idx_j == k}, sum_j f(idx_j) =
+// sum_k c_k f(k)), so the GEMMs stream contiguous 128-row chunks of kv[b]
+// instead of gathering rows; chunks past the tile's largest index are skipped
+// (with causal indexer output that is about half of the pool on average).
+//
+// B200 mapping. A tile is 128 (token, head) rows (2 tokens of 64 heads, or 1 of
+// 128); a work item is two consecutive tiles of one batch, one per softmax
+// warpgroup, which share every kv chunk. Per CTA (one per SM, persistent):
+//   warp 0      TMA: the two q tiles, then kv chunks into a 3-stage ring.
+//   warp 1      tcgen05 issuer, per chunk and tile:
+//                 S[128 x 128] = Q . KV_c^T              (8 x K16, smem operands)
+//                 O[128 x 128] += (P_hi + P_lo) . KV_c   (16 x K16, P read from TMEM)
+//   warps 2..9  two softmax warpgroups (tile 0 / tile 1 of the item). A thread
+//               owns one row: it builds the tile's per-token counts c_k in
+//               shared memory, then per chunk reads S, keeps a running max
+//               (O in TMEM is rescaled only when the max grows by more than
+//               2^8), writes P = c_k 2^(z - m) back over S as two bf16 pieces
+//               (P_hi + P_lo carries ~16 bits), and after the last chunk
+//               divides O by the running sum plus the sink term and stores.
+// TMEM per warpgroup w: S/P at columns [256w, 256w+128), O at [256w+128, 256w+256).
+// The S/P region of a chunk is reused by the next chunk only after that
+// chunk's PV product has completed (the issuer waits on its own commit).
+#include "common.cuh"
+#include "host_util.h"
+
+namespace dsa {
+namespace sal {
+
+constexpr int kRows = 128;
+constexpr int kD = 128;
+constexpr int kChunk = 128;
+constexpr int kMaxNkv = 4096;
+constexpr int kKVStages = 3;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kQBytes = kRows * kD * 2;           // 32768
+constexpr int kQBoxBytes = kRows * 64 * 2;        // 16384
+constexpr int kKVBytes = kChunk * kD * 2;         // 32768
+constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 16384
+constexpr int kCntWords = kMaxNkv / 2;            // 16-bit counters, two per word
+constexpr int kOffQ = 0;                                        // [2 wg]
+constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
+constexpr int kOffCnt = kOffKV + kKVStages * kKVBytes;          // 163840: [2 wg][2 tok]
+constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 196608
+constexpr int kOffRed = kOffMeta + 64;                          // [2 wg][4 warps] max index
+constexpr int kOffBar = kOffRed + 64;
+constexpr int kNumBars = 2 * 2 + 2 + 2 * kKVStages + 2 * 4 + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;  // O is rescaled when the max grows by more than 2^8
+
+struct Params {
+  int64_t m;               // tokens per batch
+  int heads;               // 64 or 128
+  int tpt;                 // tokens per tile
+  int tiles_per_batch;
+  int items_per_batch;
+  int64_t total_items;
+  int topk;
+  int nkv;
+  float scale_log2;
+  const float* sink;
+  const void* idx;         // [batch, m, topk] int32 / int64
+  unsigned int* err;
+};
+
+template <typename IdxT>
+__global__ void __launch_bounds__(kThreads, 1)
+    sa_long_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
+                   const __grid_constant__ CUtensorMap tm_out, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars;                       // [2] TMA -> MMA / softmax
+  uint64_t* q_empty = bars + 2;                  // [2] output stored -> producer
+  uint64_t* meta_full = bars + 4;                // [2] counts and chunk count ready
+  uint64_t* kv_full = bars + 6;                  // [kKVStages]
+  uint64_t* kv_empty = kv_full + kKVStages;      // [kKVStages]
+  uint64_t* s_full = kv_empty + kKVStages;       // [2] S of a chunk in TMEM
+  uint64_t* p_full = s_full + 2;                 // [2] P written (128 arrivals)
+  uint64_t* o_done = p_full + 2;                 // [2] PV product of a chunk completed
+  uint64_t* o_empty = o_done + 2;                // [2] O read by the epilogue (128 arrivals)
+  uint64_t* drain_bar = o_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  volatile int* meta = reinterpret_cast<volatile int*>(smem + kOffMeta);  // [2] chunks per tile
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&q_full[w], 1);
+      mbar_init(&q_empty[w], 1);
+      mbar_init(&meta_full[w], 1);
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_full[w], 128);
+      mbar_init(&o_done[w], 1);
+      mbar_init(&o_empty[w], 128);
+    }
+    for (int s = 0; s < kKVStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_kv);
+    tma_prefetch_desc(&tm_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  auto tile_of = [&](int64_t item, int w, int& b, int& tb, bool& valid) {
+    b = static_cast<int>(item / p.items_per_batch);
+    tb = static_cast<int>(item - static_cast<int64_t>(b) * p.items_per_batch) * 2 + w;
+    valid = tb < p.tiles_per_batch;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int li = 0, gc = 0;
+      bool ok = true;
+      for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
+        for (int w = 0; w < 2 && ok; ++w) {
+          int b, tb;
+          bool valid;
+          tile_of(item, w, b, tb, valid);
+          if (!mbar_wait(&q_empty[w], (li & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* qs = smem + kOffQ + w * kQBytes;
+          if (valid) {
+            mbar_arrive_expect_tx(&q_full[w], kQBytes);
+            tma_load_3d(qs, &tm_q, 0, tb * kRows, b, &q_full[w]);
+            tma_load_3d(qs + kQBoxBytes, &tm_q, 64, tb * kRows, b, &q_full[w]);
+          } else {
+            mbar_arrive(&q_full[w]);
+          }
+        }
+        if (!ok) break;
+        int nc = 0;
+        for (int w = 0; w < 2; ++w) {
+          if (!mbar_wait(&meta_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          nc = max(nc, static_cast<int>(meta[w]));
+        }
+        if (!ok) break;
+        const int b = static_cast<int>(item / p.items_per_batch);
+        for (int c = 0; c < nc; ++c, ++gc) {
+          const int s = gc % kKVStages;
+          if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* kvs = smem + kOffKV + s * kKVBytes;
+          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+          tma_load_3d(kvs, &tm_kv, 0, c * kChunk, b, &kv_full[s]);
+          tma_load_3d(kvs + kKVBoxBytes, &tm_kv, 64, c * kChunk, b, &kv_full[s]);
+        }
+      }
+      for (int i = (gc > kKVStages ? gc - kKVStages : 0); i < gc; ++i)
+        mbar_drain(&kv_full[i % kKVStages], (i / kKVStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc1 = make_idesc_bf16_f32(128, kChunk, 0, 0);
+      constexpr uint32_t idesc2 = make_idesc_bf16_f32(128, kD, 0, 1);
+      const uint32_t q_base = smem_u32(smem + kOffQ);
+      const uint32_t kv_base = smem_u32(smem + kOffKV);
+      int li = 0, gc = 0;
+      int gw[2] = {0, 0};     // chunks processed per warpgroup (all items)
+      int uses[2] = {0, 0};   // items per warpgroup that wrote O
+      bool ok = true;
+      for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
+        int ncw[2];
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (!mbar_wait(&q_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT) ||
+              !mbar_wait(&meta_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          ncw[w] = meta[w];
+        }
+        if (!ok) break;
+        const int nc = max(ncw[0], ncw[1]);
+        for (int c = 0; c < nc && ok; ++c, ++gc) {
+          const int s = gc % kKVStages;
+          if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
+          for (int w = 0; w < 2; ++w) {
+            if (c >= ncw[w]) continue;
+            // the S/P region is free once the previous chunk's PV product completed
+            if (gw[w] > 0 && !mbar_wait(&o_done[w], (gw[w] - 1) & 1, abort_flag, p.err,
+                                        DSA_DEVERR_SA_WAIT)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + static_cast<uint32_t>(w) * 256u;
+            const uint32_t qb = q_base + static_cast<uint32_t>(w) * kQBytes;
+#pragma unroll
+            for (int k = 0; k < kD / 16; ++k) {
+              const uint32_t box = static_cast<uint32_t>(k >> 2);
+              const uint32_t koff = static_cast<uint32_t>(k & 3) * 32u;
+              const uint64_t ad =
+                  make_smem_desc(qb + box * kQBoxBytes + koff, 16u, 1024u, kLayoutSW128);
+              const uint64_t bd =
+                  make_smem_desc(kvb + box * kKVBoxBytes + koff, 16u, 1024u, kLayoutSW128);
+              umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[w]);
+          }
+          if (!ok) break;
+          for (int w = 0; w < 2; ++w) {
+            if (c >= ncw[w]) continue;
+            if (!mbar_wait(&p_full[w], gw[w] & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
+              ok = false;
+              break;
+            }
+            if (c == 0) {
+              if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
+                                            DSA_DEVERR_SA_WAIT)) {
+                ok = false;
+                break;
+              }
+              ++uses[w];
+            }
+            tc_fence_after();
+            const uint32_t sp = tmem + static_cast<uint32_t>(w) * 256u;
+            const uint32_t d = sp + 128u;
+#pragma unroll
+            for (int st = 0; st < kChunk / 16; ++st) {
+              // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
+              // dim atoms (64) one box (16 KB) apart, row atoms (8) 1024 B apart.
+              const uint64_t bd = make_smem_desc(kvb + static_cast<uint32_t>(st) * 2048u,
+                                                 static_cast<uint32_t>(kKVBoxBytes), 1024u,
+                                                 kLayoutSW128);
+              // A = P in TMEM: keys [32q, 32q+32) hold P_hi in columns [32q, 32q+16)
+              // and P_lo in [32q+16, 32q+32) (two bf16 per column)
+              const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
+              umma_bf16_tmem_a(d, a_hi, bd, idesc2, (c > 0 || st > 0) ? 1u : 0u);
+              umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
+            }
+            umma_commit(&o_done[w]);
+            ++gw[w];
+          }
+          if (!ok) break;
+          umma_commit(&kv_empty[s]);
+        }
+      }
+      umma_commit(drain_bar);
+      mbar_drain(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int w = (warp - 2) >> 2;
+    const int t = threadIdx.x - 64 - 128 * w;   // 0..127
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;        // (token, head) row of the tile
+    const int tok = row / p.heads;
+    const int h = row % p.heads;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t sp = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P
+    const uint32_t od = sp + 128u;                                           // O
+    const float sink2 = p.sink[h] * kLog2e;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt) + w * 2 * kCntWords;
+    const uint32_t* my_cnt = cnt + tok * kCntWords;
+    int* red = reinterpret_cast<int*>(smem + kOffRed) + w * 4;
+    uint8_t* qs = smem + kOffQ + w * kQBytes;
+    const uint32_t bar_id = 1 + w;
+    const IdxT* idx = static_cast<const IdxT*>(p.idx);
+    // counters of whole 128-key chunks (the last chunk may run past n_kv)
+    const int nkv_words = ((p.nkv + kChunk - 1) / kChunk) * (kChunk / 2);
+    bool ok = true;
+    int li = 0, g = 0;
+    for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++li) {
+      int b, tb;
+      bool valid;
+      tile_of(item, w, b, tb, valid);
+      // ---- counts of this tile's tokens and the number of chunks to visit
+      int maxidx = -1;
+      if (valid) {
+        for (int i = t; i < p.tpt * nkv_words; i += 128)
+          cnt[(i / nkv_words) * kCntWords + (i % nkv_words)] = 0u;
+        named_bar_sync(bar_id, 128);
+        const int64_t tok0 = static_cast<int64_t>(tb) * kRows / p.heads;
+        const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
+        const int n_ent = p.tpt * p.topk;
+        for (int i = t; i < n_ent; i += 128) {
+          const int64_t k = static_cast<int64_t>(__ldg(src + i));
+          if (k >= 0 && k < p.nkv) {
+            const int kk = static_cast<int>(k);
+            atomicAdd(&cnt[(i / p.topk) * kCntWords + (kk >> 1)], 1u << ((kk & 1) * 16));
+            maxidx = max(maxidx, kk);
+          }
+        }
+      }
+      maxidx = __reduce_max_sync(0xFFFFFFFFu, maxidx);
+      if (lane == 0) red[quarter] = maxidx;
+      named_bar_sync(bar_id, 128);
+      const int mx_all = max(max(red[0], red[1]), max(red[2], red[3]));
+      const int nc = valid ? (mx_all + kChunk) / kChunk : 0;  // chunks holding any counted row
+      if (t == 0) {
+        meta[w] = nc;
+        mbar_arrive(&meta_full[w]);
+      }
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&q_full[w], li & 1, abort_flag, p.err,
+                                             DSA_DEVERR_SA_WAIT));
+      // ---- chunks
+      float m_run = sink2, l_run = 0.f;
+      for (int c = 0; ok && c < nc; ++c, ++g) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], g & 1, abort_flag, p.err,
+                                               DSA_DEVERR_SA_WAIT));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t* cw = my_cnt + c * (kChunk / 2);
+        // pass 1: chunk max over the counted keys
+        float mx = -INFINITY;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), sv);
+          uint32_t cv[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v = reinterpret_cast<const uint4*>(cw + q4 * 16)[j];
+            cv[4 * j] = v.x; cv[4 * j + 1] = v.y; cv[4 * j + 2] = v.z; cv[4 * j + 3] = v.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const uint32_t ck = (cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu;
+            if (ck) mx = fmaxf(mx, __uint_as_float(sv[k]) * p.scale_log2);
+          }
+        }
+        // running max; O is rescaled only when the max grows by more than 2^8
+        float factor = 1.f;
+        if (c == 0) {
+          m_run = fmaxf(m_run, mx);
+        } else if (mx > m_run + kRescaleLog2) {
+          factor = exp2f(m_run - mx);
+          m_run = mx;
+          l_run *= factor;
+        }
+        if (c > 0 && __any_sync(0xFFFFFFFFu, factor != 1.f)) {
+          // O holds the previous chunk's product once it has completed
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
+                                                 DSA_DEVERR_SA_WAIT));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) ov[k] = __float_as_uint(__uint_as_float(ov[k]) * factor);
+            tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
+          }
+        }
+        // pass 2: P = c_k 2^(z - m) as bf16 hi + lo, written over the S columns
+        // of the same 32 keys (consumed just before)
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), sv);
+          uint32_t cv[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v = reinterpret_cast<const uint4*>(cw + q4 * 16)[j];
+            cv[4 * j] = v.x; cv[4 * j + 1] = v.y; cv[4 * j + 2] = v.z; cv[4 * j + 3] = v.w;
+          }
+          uint32_t pk[32];
+#pragma unroll
+          for (int k2 = 0; k2 < 16; ++k2) {
+            float e[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int k = 2 * k2 + u;
+              const uint32_t ck = (cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu;
+              const float z = __uint_as_float(sv[k]) * p.scale_log2;
+              e[u] = ck ? static_cast<float>(ck) * exp2f(z - m_run) : 0.f;
+              l_run += e[u];
+            }
+            const uint32_t hi = pack_bf16x2(e[0], e[1]);
+            pk[k2] = hi;
+            pk[16 + k2] = pack_bf16x2(e[0] - bf16_bits_to_float(hi & 0xFFFFu),
+                                      e[1] - bf16_bits_to_float(hi >> 16));
+          }
+          tmem_st_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), pk);
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full[w]);
+      }
+      // ---- epilogue: O / (l + sink term) -> bf16 -> q buffer (SW128) -> TMA store
+      if (ok && nc > 0) {
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
+                                               DSA_DEVERR_SA_WAIT));
+      }
+      if (ok && valid) {
+        const float inv = 1.0f / (l_run + exp2f(sink2 - m_run));
+        if (nc > 0) tc_fence_after();
+        const uint32_t ob_row = smem_u32(qs) + static_cast<uint32_t>(row) * 128u;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t ov[32];
+          if (nc > 0) {
+            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(cc) * 32u, ov);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) ov[k] = 0u;  // only the sink: the output is 0
+          }
+          const uint32_t box_addr = ob_row + static_cast<uint32_t>(cc >> 1) * kQBoxBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t chunk = static_cast<uint32_t>((cc & 1) * 4 + j);
+            uint32_t wv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              wv[u] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * u]) * inv,
+                                  __uint_as_float(ov[8 * j + 2 * u + 1]) * inv);
+            st_shared_v4(box_addr + ((chunk ^ static_cast<uint32_t>(row & 7)) << 4), wv[0], wv[1],
+                         wv[2], wv[3]);
+          }
+        }
+        if (nc > 0) {
+          tc_fence_before();
+          mbar_arrive(&o_empty[w]);
+        }
+        fence_proxy_async_smem();
+      }
+      if (!named_bar_and(bar_id, 128, ok)) break;
+      if (t == 0) {
+        if (valid) {
+          tma_store_3d(&tm_out, qs, 0, tb * kRows, b);
+          tma_store_3d(&tm_out, qs + kQBoxBytes, 64, tb * kRows, b);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();
+        }
+        mbar_arrive(&q_empty[w]);
+      }
+    }
+    if (t == 0) bulk_wait_group<0>();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename IdxT>
+int launch(const void* q, const void* kv, const void* idx, const float* sink, void* out,
+           int64_t batch, int64_t m, int heads, int nkv, int topk, float scale,
+           cudaStream_t stream) {
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st != DSA_OK) return st;
+  if (di.max_smem_optin < kSmemBytes) return DSA_ERR_UNSUPPORTED;
+  unsigned int* err = nullptr;
+  st = device_error_word(&err);
+  if (st != DSA_OK) return st;
+  const int64_t rows = m * heads;
+  if (rows % kRows != 0) return DSA_ERR_UNSUPPORTED;  // whole tokens per tile
+  const int64_t tiles = rows / kRows;
+  const int64_t items_pb = (tiles + 1) / 2;
+  if (tiles > 0x7FFFFFFF || batch * items_pb > (int64_t{1} << 40)) return DSA_ERR_UNSUPPORTED;
+  CUtensorMap tm_q, tm_kv, tm_out;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(rows),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2,
+                                 static_cast<uint64_t>(rows) * kD * 2};
+    const uint32_t box[3] = {64, kRows, 1};
+    st = encode_tensor_map(&tm_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DSA_OK) return st;
+    st = encode_tensor_map(&tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DSA_OK) return st;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kD), static_cast<uint64_t>(nkv),
+                              static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(kD) * 2,
+                                 static_cast<uint64_t>(nkv) * kD * 2};
+    const uint32_t box[3] = {64, kChunk, 1};
+    st = encode_tensor_map(&tm_kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, kv, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != DSA_OK) return st;
+  }
+  Params p;
+  p.m = m;
+  p.heads = heads;
+  p.tpt = kRows / heads;
+  p.tiles_per_batch = static_cast<int>(tiles);
+  p.items_per_batch = static_cast<int>(items_pb);
+  p.total_items = items_pb * batch;
+  p.topk = topk;
+  p.nkv = nkv;
+  p.scale_log2 = scale * kLog2e;
+  p.sink = sink;
+  p.idx = idx;
+  p.err = err;
+  static bool attr_done[64] = {false};
+  if (!attr_done[di.device]) {
+    st = cuda_status(cudaFuncSetAttribute(sa_long_kernel<int32_t>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    if (st == DSA_OK)
+      st = cuda_status(cudaFuncSetAttribute(sa_long_kernel<int64_t>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kSmemBytes));
+    if (st != DSA_OK) return st;
+    attr_done[di.device] = true;
+  }
+  const int64_t grid64 = p.total_items < di.num_sms ? p.total_items : di.num_sms;
+  sa_long_kernel<IdxT><<<static_cast<unsigned>(grid64), kThreads, kSmemBytes, stream>>>(
+      tm_q, tm_kv, tm_out, p);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace sal
+
+// Long-pool SparseAttention: heads in {64, 128}, head_dim 128, n_kv <= 4096.
+bool sa_long_supported(int heads, int head_dim, int nkv) {
+  return (heads == 64 || heads == 128) && head_dim == sal::kD && nkv >= 1 && nkv <= sal::kMaxNkv;
+}
+
+int launch_sa_long(const void* q, const void* kv, const void* idx, int idx_elem_bytes,
+                   const float* sink, void* out, int64_t batch, int64_t m, int heads, int nkv,
+                   int topk, float scale, cudaStream_t stream) {
+  if (idx_elem_bytes == 8)
+    return sal::launch<int64_t>(q, kv, idx, sink, out, batch, m, heads, nkv, topk, scale, stream);
+  return sal::launch<int32_t>(q, kv, idx, sink, out, batch, m, heads, nkv, topk, scale, stream);
+}
+
+}  // namespace dsa

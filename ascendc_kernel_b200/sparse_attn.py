@@ -25,9 +25,11 @@ def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
                 out: torch.Tensor | None = None) -> torch.Tensor:
     """out[b,t,h] = sum_j softmax_j(q.kv[idx_j] * scale ++ sink[h]) kv[idx_j].
 
-    q [b, m, h, 128] bf16, kv [b, n_kv <= 32, 128] bf16, topk_idxs [b, m, topk]
+    q [b, m, h, 128] bf16, kv [b, n_kv, 128] bf16, topk_idxs [b, m, topk]
     int32 or int64 (negative = masked), attn_sink [h] fp32. Returns bf16 like q.
     Same semantics as ``sparse_attn_ref`` (reference/task1_v0_ref.py:5-24).
+    Two kernels: n_kv <= 32 with topk <= 128 (the BASELINE shape), and a chunked
+    one for long kv pools (n_kv <= 4096, any topk, 64 or 128 heads).
     """
     assert q.is_cuda and kv.is_cuda and topk_idxs.is_cuda, "inputs must be CUDA tensors"
     assert q.dtype == torch.bfloat16 and kv.dtype == torch.bfloat16, "q and kv must be bf16"
@@ -37,10 +39,13 @@ def sparse_attn(q: torch.Tensor, kv: torch.Tensor, attn_sink: torch.Tensor,
     assert topk_idxs.shape[:2] == (b, m), "topk_idxs must be [b, m, topk]"
     assert d == 128, "kernel specialised to head_dim == 128"
     assert h in SUPPORTED_HEADS, f"kernel specialised to n_heads in {SUPPORTED_HEADS}"
-    assert kv.shape[1] <= 32, "kernel specialised to n_kv <= 32"
     topk = topk_idxs.shape[-1]
-    assert (topk * topk_idxs.element_size()) % 16 == 0 and topk <= 128, \
-        "topk * sizeof(index) must be a multiple of 16 bytes and topk <= 128"
+    if kv.shape[1] <= 32 and topk <= 128:
+        assert (topk * topk_idxs.element_size()) % 16 == 0, \
+            "topk * sizeof(index) must be a multiple of 16 bytes"
+    else:
+        assert kv.shape[1] <= 4096 and h in (64, 128), \
+            "long kv pools: n_kv <= 4096 and n_heads in (64, 128)"
     q = q.contiguous()
     kv = kv.contiguous()
     topk_idxs = topk_idxs.contiguous()

@@ -58,9 +58,10 @@ def sa(**kw):
     (dict(eb=2), INVALID),
     (dict(d=64), UNSUPPORTED),
     (dict(h=48), UNSUPPORTED),
-    (dict(nkv=33), UNSUPPORTED),
+    (dict(nkv=33, h=16), UNSUPPORTED),    # long kv pools need 64 or 128 heads
+    (dict(nkv=4097), UNSUPPORTED),        # long kv pools: at most 4096 rows
     (dict(topk=6), UNSUPPORTED),          # 24 bytes: not a multiple of 16
-    (dict(topk=256), UNSUPPORTED),
+    (dict(topk=256, h=32), UNSUPPORTED),
     (dict(q=FAKE + 2), MISALIGNED),
     (dict(b=0), OK),                      # empty batch is a no-op
     (dict(m=0), OK),

@@ -22,13 +22,13 @@ ATOL = RTOL = 1e-2
 MAX_MISMATCH_FRAC = 1e-3
 
 
-def run_and_compare(q, kv, idx, sink, scale, dev):
+def run_and_compare(q, kv, idx, sink, scale, dev, max_frac=MAX_MISMATCH_FRAC):
     out = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), scale)
     got = to_u16(out)
     want = oracle.sparse_attn(to_u16(q), to_u16(kv), idx.numpy(), sink.numpy(), scale)
     r = bf16_compare(got, want, ATOL, RTOL)
     assert r["allclose"], r
-    assert r["bit_mismatch"] <= max(4, r["n"] * MAX_MISMATCH_FRAC), r
+    assert r["bit_mismatch"] <= max(4, r["n"] * max_frac), r
     assert _native.device_error(dev.index) == 0
     return r, got
 
@@ -103,3 +103,49 @@ def test_int64_chained_indices_equal_int32(cuda_device):
     a = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.to(dev), 0.1)
     b = sa.sparse_attn(q.to(dev), kv.to(dev), sink.to(dev), idx.long().to(dev), 0.1)
     assert torch.equal(a, b)
+
+
+# The long-pool kernel carries P as two bf16 pieces (~16 bits): about 2^-8 of
+# outputs that sit near a bf16 rounding boundary land one ulp away from the
+# correctly rounded fp64 result (measured ~0.25 %); still within atol = rtol =
+# 1e-2, the reference harness's tolerance.
+LONG_MAX_MISMATCH_FRAC = 1e-2
+
+
+def make_long(b, m, h, nkv, topk, dtype, seed, masked_frac=0.2, dup=False, bound=None):
+    """Long kv pool: distinct indices per token (like top-k output) below `bound`,
+    a fraction replaced by -1; with dup, indices drawn with replacement."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, m, h, 128, generator=g).to(torch.bfloat16)
+    kv = torch.randn(b, nkv, 128, generator=g).to(torch.bfloat16)
+    hi = bound or nkv
+    if dup:
+        idx = torch.randint(0, hi, (b, m, topk), generator=g)
+    else:
+        idx = torch.stack([torch.stack([torch.randperm(max(hi, topk), generator=g)[:topk]
+                                        for _ in range(m)]) for _ in range(b)])
+        idx = torch.where(idx < hi, idx, torch.full_like(idx, -1))
+    drop = torch.rand(b, m, topk, generator=g) < masked_frac
+    idx = torch.where(drop, torch.full_like(idx, -1), idx).to(dtype)
+    sink = torch.randn(h, generator=g) * 0.5
+    return q, kv, idx, sink
+
+
+@pytest.mark.parametrize("b,m,h,nkv,topk,dtype,dup,bound", [
+    (1, 6, 64, 256, 128, torch.int32, False, None),    # 3 tiles: one item has an empty tile
+    (2, 8, 64, 512, 300, torch.int64, True, None),     # duplicates (multiplicity > 1)
+    (1, 4, 128, 1000, 512, torch.int32, False, None),  # 128 heads, n_kv not a multiple of 128
+    (1, 8, 64, 4096, 2048, torch.int32, False, 2600),  # indexer-like: rows < 2600 only
+    (2, 4, 64, 4096, 2048, torch.int64, False, None),  # the chained configuration's shapes
+])
+def test_long_kv_pool(cuda_device, b, m, h, nkv, topk, dtype, dup, bound):
+    q, kv, idx, sink = make_long(b, m, h, nkv, topk, dtype, seed=nkv + topk, dup=dup, bound=bound)
+    r, _ = run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device, LONG_MAX_MISMATCH_FRAC)
+    assert r["max_abs"] <= 4e-3, r
+
+
+def test_long_kv_pool_all_masked_token(cuda_device):
+    q, kv, idx, sink = make_long(1, 4, 64, 1024, 256, torch.int32, seed=9)
+    idx[0, 1] = -1  # token 1 attends to the sink only: output 0
+    r, got = run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device, LONG_MAX_MISMATCH_FRAC)
+    assert np.all(got.reshape(1, 4, 64, 128)[0, 1] == 0)
