@@ -7,7 +7,7 @@
 //   mx  = max(max_j s_j, sink[h])
 //   out = sum_j exp(s_j - mx) kv[b, idx_j] / (sum_j exp(s_j - mx) + exp(sink[h] - mx))
 // in the multiplicity form (c_k = #{j : idx_j == k}, sum_j f(idx_j) =
-// sum_k c_k f(k)), so the GEMMs stream contiguous 128-row chunks of kv[b]
+// sum_k c_k f(k)), so the GEMMs stream contiguous 64-row chunks of kv[b]
 // instead of gathering rows; chunks past the tile's largest index are skipped
 // (with causal indexer output that is about half of the pool on average).
 //
@@ -16,8 +16,8 @@
 // warpgroup, which share every kv chunk. Per CTA (one per SM, persistent):
 //   warp 0      TMA: the two q tiles, then kv chunks into a 3-stage ring.
 //   warp 1      tcgen05 issuer, per chunk and tile:
-//                 S[128 x 128] = Q . KV_c^T              (8 x K16, smem operands)
-//                 O[128 x 128] += (P_hi + P_lo) . KV_c   (16 x K16, P read from TMEM)
+//                 S[128 x 64]  = Q . KV_c^T              (8 x K16, smem operands)
+//                 O[128 x 128] += (P_hi + P_lo) . KV_c   (8 x K16, P read from TMEM)
 //   warps 2..9  two softmax warpgroups (tile 0 / tile 1 of the item). A thread
 //               owns one row: it builds the tile's per-token counts c_k in
 //               shared memory, then per chunk reads S, keeps a running max
@@ -25,9 +25,11 @@
 //               2^8), writes P = c_k 2^(z - m) back over S as two bf16 pieces
 //               (P_hi + P_lo carries ~16 bits), and after the last chunk
 //               divides O by the running sum plus the sink term and stores.
-// TMEM per warpgroup w: S/P at columns [256w, 256w+128), O at [256w+128, 256w+256).
-// The S/P region of a chunk is reused by the next chunk only after that
-// chunk's PV product has completed (the issuer waits on its own commit).
+// Chunks are 64 kv rows. TMEM per warpgroup w: two S/P buffers at columns
+// [256w, 256w+64) and [256w+64, 256w+128), O at [256w+128, 256w+256). An S/P
+// buffer is reused two chunks later, once that chunk's PV product completed
+// (the issuer waits on its own commit), so QK^T of chunk c+1 overlaps the
+// softmax of chunk c.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -36,23 +38,23 @@ namespace sal {
 
 constexpr int kRows = 128;
 constexpr int kD = 128;
-constexpr int kChunk = 128;
+constexpr int kChunk = 64;
 constexpr int kMaxNkv = 4096;
-constexpr int kKVStages = 3;
+constexpr int kKVStages = 4;
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kQBytes = kRows * kD * 2;           // 32768
 constexpr int kQBoxBytes = kRows * 64 * 2;        // 16384
-constexpr int kKVBytes = kChunk * kD * 2;         // 32768
-constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 16384
+constexpr int kKVBytes = kChunk * kD * 2;         // 16384
+constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 8192
 constexpr int kCntWords = kMaxNkv / 2;            // 16-bit counters, two per word
 constexpr int kOffQ = 0;                                        // [2 wg]
 constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
-constexpr int kOffCnt = kOffKV + kKVStages * kKVBytes;          // 163840: [2 wg][2 tok]
-constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 196608
+constexpr int kOffCnt = kOffKV + kKVStages * kKVBytes;          // 131072: [2 wg][2 tok]
+constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 163840
 constexpr int kOffRed = kOffMeta + 64;                          // [2 wg][4 warps] max index
 constexpr int kOffBar = kOffRed + 64;
-constexpr int kNumBars = 2 * 2 + 2 + 2 * kKVStages + 2 * 4 + 1;
+constexpr int kNumBars = 2 * 3 + 2 * kKVStages + 2 * 2 * 3 + 2 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -86,10 +88,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* meta_full = bars + 4;                // [2] counts and chunk count ready
   uint64_t* kv_full = bars + 6;                  // [kKVStages]
   uint64_t* kv_empty = kv_full + kKVStages;      // [kKVStages]
-  uint64_t* s_full = kv_empty + kKVStages;       // [2] S of a chunk in TMEM
-  uint64_t* p_full = s_full + 2;                 // [2] P written (128 arrivals)
-  uint64_t* o_done = p_full + 2;                 // [2] PV product of a chunk completed
-  uint64_t* o_empty = o_done + 2;                // [2] O read by the epilogue (128 arrivals)
+  // per warpgroup w and S buffer j: index [2 w + j]
+  uint64_t* s_full = kv_empty + kKVStages;       // [4] S of a chunk in TMEM
+  uint64_t* p_full = s_full + 4;                 // [4] P written (128 arrivals)
+  uint64_t* o_done = p_full + 4;                 // [4] PV product of the buffer's chunk done
+  uint64_t* o_empty = o_done + 4;                // [2] O read by the epilogue (128 arrivals)
   uint64_t* drain_bar = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
@@ -103,10 +106,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_full[w], 1);
       mbar_init(&q_empty[w], 1);
       mbar_init(&meta_full[w], 1);
-      mbar_init(&s_full[w], 1);
-      mbar_init(&p_full[w], 128);
-      mbar_init(&o_done[w], 1);
       mbar_init(&o_empty[w], 128);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -188,13 +193,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Per chunk c: S of chunk c for both tiles (into S buffer c % 2, free once
+    // the PV product of chunk c - 2 completed), then the PV products of chunk
+    // c - 1; so the softmax of one chunk overlaps the QK^T of the next.
     if (lane == 0) {
       constexpr uint32_t idesc1 = make_idesc_bf16_f32(128, kChunk, 0, 0);
       constexpr uint32_t idesc2 = make_idesc_bf16_f32(128, kD, 0, 1);
       const uint32_t q_base = smem_u32(smem + kOffQ);
       const uint32_t kv_base = smem_u32(smem + kOffKV);
       int li = 0, gc = 0;
-      int gw[2] = {0, 0};     // chunks processed per warpgroup (all items)
+      int gs[2] = {0, 0};     // S products issued per warpgroup (all items)
+      int gm[2] = {0, 0};     // PV products issued per warpgroup
       int uses[2] = {0, 0};   // items per warpgroup that wrote O
       bool ok = true;
       for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
@@ -209,73 +218,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         const int nc = max(ncw[0], ncw[1]);
-        for (int c = 0; c < nc && ok; ++c, ++gc) {
-          const int s = gc % kKVStages;
-          if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
-                         DSA_DEVERR_SA_WAIT)) {
-            ok = false;
-            break;
-          }
-          const uint32_t kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
-          for (int w = 0; w < 2; ++w) {
-            if (c >= ncw[w]) continue;
-            // the S/P region is free once the previous chunk's PV product completed
-            if (gw[w] > 0 && !mbar_wait(&o_done[w], (gw[w] - 1) & 1, abort_flag, p.err,
-                                        DSA_DEVERR_SA_WAIT)) {
+        uint32_t prev_kvb = 0;
+        int prev_s = 0;
+        for (int c = 0; c <= nc && ok; ++c) {
+          uint32_t kvb = 0;
+          int s = 0;
+          if (c < nc) {
+            s = gc % kKVStages;
+            if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
+                           DSA_DEVERR_SA_WAIT)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t d = tmem + static_cast<uint32_t>(w) * 256u;
-            const uint32_t qb = q_base + static_cast<uint32_t>(w) * kQBytes;
-#pragma unroll
-            for (int k = 0; k < kD / 16; ++k) {
-              const uint32_t box = static_cast<uint32_t>(k >> 2);
-              const uint32_t koff = static_cast<uint32_t>(k & 3) * 32u;
-              const uint64_t ad =
-                  make_smem_desc(qb + box * kQBoxBytes + koff, 16u, 1024u, kLayoutSW128);
-              const uint64_t bd =
-                  make_smem_desc(kvb + box * kKVBoxBytes + koff, 16u, 1024u, kLayoutSW128);
-              umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[w]);
-          }
-          if (!ok) break;
-          for (int w = 0; w < 2; ++w) {
-            if (c >= ncw[w]) continue;
-            if (!mbar_wait(&p_full[w], gw[w] & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
-              ok = false;
-              break;
-            }
-            if (c == 0) {
-              if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
-                                            DSA_DEVERR_SA_WAIT)) {
+            ++gc;
+            kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
+            for (int w = 0; w < 2; ++w) {
+              if (c >= ncw[w]) continue;
+              const int j = gs[w] & 1;
+              if (gs[w] >= 2 && !mbar_wait(&o_done[2 * w + j], ((gs[w] >> 1) + 1) & 1, abort_flag,
+                                           p.err, DSA_DEVERR_SA_WAIT)) {
                 ok = false;
                 break;
               }
-              ++uses[w];
-            }
-            tc_fence_after();
-            const uint32_t sp = tmem + static_cast<uint32_t>(w) * 256u;
-            const uint32_t d = sp + 128u;
+              tc_fence_after();
+              const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
+              const uint32_t qb = q_base + static_cast<uint32_t>(w) * kQBytes;
 #pragma unroll
-            for (int st = 0; st < kChunk / 16; ++st) {
-              // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
-              // dim atoms (64) one box (16 KB) apart, row atoms (8) 1024 B apart.
-              const uint64_t bd = make_smem_desc(kvb + static_cast<uint32_t>(st) * 2048u,
-                                                 static_cast<uint32_t>(kKVBoxBytes), 1024u,
-                                                 kLayoutSW128);
-              // A = P in TMEM: keys [32q, 32q+32) hold P_hi in columns [32q, 32q+16)
-              // and P_lo in [32q+16, 32q+32) (two bf16 per column)
-              const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
-              umma_bf16_tmem_a(d, a_hi, bd, idesc2, (c > 0 || st > 0) ? 1u : 0u);
-              umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
+              for (int k = 0; k < kD / 16; ++k) {
+                const uint32_t box = static_cast<uint32_t>(k >> 2);
+                const uint32_t koff = static_cast<uint32_t>(k & 3) * 32u;
+                const uint64_t ad =
+                    make_smem_desc(qb + box * kQBoxBytes + koff, 16u, 1024u, kLayoutSW128);
+                const uint64_t bd =
+                    make_smem_desc(kvb + box * kKVBoxBytes + koff, 16u, 1024u, kLayoutSW128);
+                umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
+              }
+              umma_commit(&s_full[2 * w + j]);
+              ++gs[w];
             }
-            umma_commit(&o_done[w]);
-            ++gw[w];
+            if (!ok) break;
           }
-          if (!ok) break;
-          umma_commit(&kv_empty[s]);
+          if (c >= 1) {
+            const int cp = c - 1;  // PV products of the previous chunk
+            for (int w = 0; w < 2; ++w) {
+              if (cp >= ncw[w]) continue;
+              const int j = gm[w] & 1;
+              if (!mbar_wait(&p_full[2 * w + j], (gm[w] >> 1) & 1, abort_flag, p.err,
+                             DSA_DEVERR_SA_WAIT)) {
+                ok = false;
+                break;
+              }
+              if (cp == 0) {
+                if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
+                                              DSA_DEVERR_SA_WAIT)) {
+                  ok = false;
+                  break;
+                }
+                ++uses[w];
+              }
+              tc_fence_after();
+              const uint32_t sp = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
+              const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + 2 * kChunk);
+#pragma unroll
+              for (int st = 0; st < kChunk / 16; ++st) {
+                // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
+                // dim atoms (64) one box apart, row atoms (8) 1024 B apart.
+                const uint64_t bd = make_smem_desc(prev_kvb + static_cast<uint32_t>(st) * 2048u,
+                                                   static_cast<uint32_t>(kKVBoxBytes), 1024u,
+                                                   kLayoutSW128);
+                // A = P in TMEM: keys [32h, 32h+32) hold P_hi in columns [32h, 32h+16)
+                // and P_lo in [32h+16, 32h+32) (two bf16 per column)
+                const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
+                umma_bf16_tmem_a(d, a_hi, bd, idesc2, (cp > 0 || st > 0) ? 1u : 0u);
+                umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
+              }
+              umma_commit(&o_done[2 * w + j]);
+              ++gm[w];
+            }
+            if (!ok) break;
+            umma_commit(&kv_empty[prev_s]);
+          }
+          prev_kvb = kvb;
+          prev_s = s;
         }
       }
       umma_commit(drain_bar);
@@ -290,8 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok = row / p.heads;
     const int h = row % p.heads;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t sp = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P
-    const uint32_t od = sp + 128u;                                           // O
+    const uint32_t sp0 = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P buffers
+    const uint32_t od = sp0 + 2u * kChunk;                                    // O
     const float sink2 = p.sink[h] * kLog2e;
     uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt) + w * 2 * kCntWords;
     const uint32_t* my_cnt = cnt + tok * kCntWords;
@@ -310,18 +334,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- counts of this tile's tokens and the number of chunks to visit
       int maxidx = -1;
       if (valid) {
-        for (int i = t; i < p.tpt * nkv_words; i += 128)
-          cnt[(i / nkv_words) * kCntWords + (i % nkv_words)] = 0u;
+        for (int i = t * 4; i < p.tpt * nkv_words; i += 128 * 4)  // nkv_words % 32 == 0
+          *reinterpret_cast<uint4*>(&cnt[(i / nkv_words) * kCntWords + (i % nkv_words)]) =
+              make_uint4(0, 0, 0, 0);
         named_bar_sync(bar_id, 128);
         const int64_t tok0 = static_cast<int64_t>(tb) * kRows / p.heads;
         const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
         const int n_ent = p.tpt * p.topk;
-        for (int i = t; i < n_ent; i += 128) {
-          const int64_t k = static_cast<int64_t>(__ldg(src + i));
-          if (k >= 0 && k < p.nkv) {
-            const int kk = static_cast<int>(k);
-            atomicAdd(&cnt[(i / p.topk) * kCntWords + (kk >> 1)], 1u << ((kk & 1) * 16));
-            maxidx = max(maxidx, kk);
+        // batches of 8 independent loads ahead of their shared-memory atomics
+        for (int i0 = 0; i0 < n_ent; i0 += 8 * 128) {
+          int64_t kb[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * 128 + t;
+            kb[u] = i < n_ent ? static_cast<int64_t>(__ldg(src + i)) : -1;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int64_t k = kb[u];
+            if (k >= 0 && k < p.nkv) {
+              const int i = i0 + u * 128 + t;
+              const int kk = static_cast<int>(k);
+              atomicAdd(&cnt[(i / p.topk) * kCntWords + (kk >> 1)], 1u << ((kk & 1) * 16));
+              maxidx = max(maxidx, kk);
+            }
           }
         }
       }
@@ -339,42 +375,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- chunks
       float m_run = sink2, l_run = 0.f;
       for (int c = 0; ok && c < nc; ++c, ++g) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], g & 1, abort_flag, p.err,
-                                               DSA_DEVERR_SA_WAIT));
+        const int j = g & 1;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[2 * w + j], (g >> 1) & 1, abort_flag,
+                                               p.err, DSA_DEVERR_SA_WAIT));
         if (!ok) break;
         tc_fence_after();
+        const uint32_t sp = sp0 + static_cast<uint32_t>(j * kChunk);
         const uint32_t* cw = my_cnt + c * (kChunk / 2);
-        // pass 1: chunk max over the counted keys
+        // the chunk's 64 scores in registers, one read of S
+        uint32_t sv[kChunk];
+        tmem_ld_32x32b_x32(sp, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld_32x32b_x32(sp + 32u, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        // counts: 16 bits per key, read from shared memory (a broadcast) per 8 keys
         float mx = -INFINITY;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), sv);
-          uint32_t cv[16];
+        for (int q4 = 0; q4 < kChunk / 8; ++q4) {
+          const uint4 v = reinterpret_cast<const uint4*>(cw)[q4];
+          const uint32_t cv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 v = reinterpret_cast<const uint4*>(cw + q4 * 16)[j];
-            cv[4 * j] = v.x; cv[4 * j + 1] = v.y; cv[4 * j + 2] = v.z; cv[4 * j + 3] = v.w;
-          }
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const uint32_t ck = (cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu;
-            if (ck) mx = fmaxf(mx, __uint_as_float(sv[k]) * p.scale_log2);
+          for (int k = 0; k < 8; ++k) {
+            if ((cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu)
+              mx = fmaxf(mx, __uint_as_float(sv[8 * q4 + k]));
           }
         }
+        mx *= p.scale_log2;  // scale > 0: the max of the scaled scores
         // running max; O is rescaled only when the max grows by more than 2^8
         float factor = 1.f;
         if (c == 0) {
           m_run = fmaxf(m_run, mx);
         } else if (mx > m_run + kRescaleLog2) {
-          factor = exp2f(m_run - mx);
+          factor = ex2_approx(m_run - mx);
           m_run = mx;
           l_run *= factor;
         }
         if (c > 0 && __any_sync(0xFFFFFFFFu, factor != 1.f)) {
-          // O holds the previous chunk's product once it has completed
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
-                                                 DSA_DEVERR_SA_WAIT));
+          // O holds every earlier chunk's product once the last one completed
+          const int jp = (g - 1) & 1;
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[2 * w + jp], ((g - 1) >> 1) & 1,
+                                                 abort_flag, p.err, DSA_DEVERR_SA_WAIT));
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
@@ -386,47 +424,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
           }
         }
-        // pass 2: P = c_k 2^(z - m) as bf16 hi + lo, written over the S columns
-        // of the same 32 keys (consumed just before)
+        // P = c_k 2^(z - m) as bf16 hi + lo over the S columns of the same keys:
+        // keys [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in [32h+16, 32h+32)
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), sv);
-          uint32_t cv[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 v = reinterpret_cast<const uint4*>(cw + q4 * 16)[j];
-            cv[4 * j] = v.x; cv[4 * j + 1] = v.y; cv[4 * j + 2] = v.z; cv[4 * j + 3] = v.w;
-          }
+        for (int hh = 0; hh < kChunk / 32; ++hh) {
           uint32_t pk[32];
 #pragma unroll
           for (int k2 = 0; k2 < 16; ++k2) {
+            const uint32_t cword = cw[hh * 16 + k2];
             float e[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              const int k = 2 * k2 + u;
-              const uint32_t ck = (cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu;
-              const float z = __uint_as_float(sv[k]) * p.scale_log2;
-              e[u] = ck ? static_cast<float>(ck) * exp2f(z - m_run) : 0.f;
-              l_run += e[u];
+              const int k = hh * 32 + 2 * k2 + u;
+              const uint32_t ck = (cword >> (u * 16)) & 0xFFFFu;
+              const float z = fmaf(__uint_as_float(sv[k]), p.scale_log2, -m_run);
+              // exact float of the count (< 2^23) without a conversion instruction
+              const float ckf = __uint_as_float(0x4B000000u | ck) - 8388608.0f;
+              e[u] = ck ? ckf * ex2_approx(z) : 0.f;
+              ls[(k2 & 1) * 2 + u] += e[u];
             }
             const uint32_t hi = pack_bf16x2(e[0], e[1]);
             pk[k2] = hi;
             pk[16 + k2] = pack_bf16x2(e[0] - bf16_bits_to_float(hi & 0xFFFFu),
                                       e[1] - bf16_bits_to_float(hi >> 16));
           }
-          tmem_st_32x32b_x32(sp + static_cast<uint32_t>(q4 * 32), pk);
+          tmem_st_32x32b_x32_nowait(sp + static_cast<uint32_t>(hh * 32), pk);
         }
+        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[w]);
+        mbar_arrive(&p_full[2 * w + j]);
       }
       // ---- epilogue: O / (l + sink term) -> bf16 -> q buffer (SW128) -> TMA store
       if (ok && nc > 0) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
-                                               DSA_DEVERR_SA_WAIT));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[2 * w + ((g - 1) & 1)], ((g - 1) >> 1) & 1,
+                                               abort_flag, p.err, DSA_DEVERR_SA_WAIT));
       }
       if (ok && valid) {
-        const float inv = 1.0f / (l_run + exp2f(sink2 - m_run));
+        const float inv = 1.0f / (l_run + ex2_approx(sink2 - m_run));
         if (nc > 0) tc_fence_after();
         const uint32_t ob_row = smem_u32(qs) + static_cast<uint32_t>(row) * 128u;
 #pragma unroll
