@@ -47,11 +47,11 @@ constexpr int kQBytes = kRows * kD * 2;           // 32768
 constexpr int kQBoxBytes = kRows * 64 * 2;        // 16384
 constexpr int kKVBytes = kChunk * kD * 2;         // 16384
 constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 8192
-constexpr int kCntWords = kMaxNkv / 2;            // 16-bit counters, two per word
+constexpr int kCntWords = kMaxNkv;                // a count, then log2(count), per key
 constexpr int kOffQ = 0;                                        // [2 wg]
 constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
 constexpr int kOffCnt = kOffKV + kKVStages * kKVBytes;          // 131072: [2 wg][2 tok]
-constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 163840
+constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 196608
 constexpr int kOffRed = kOffMeta + 64;                          // [2 wg][4 warps] max index
 constexpr int kOffBar = kOffRed + 64;
 constexpr int kNumBars = 2 * 3 + 2 * kKVStages + 2 * 2 * 3 + 2 + 1;
@@ -318,13 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t od = sp0 + 2u * kChunk;                                    // O
     const float sink2 = p.sink[h] * kLog2e;
     uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt) + w * 2 * kCntWords;
-    const uint32_t* my_cnt = cnt + tok * kCntWords;
+    const float* my_bias = reinterpret_cast<const float*>(cnt + tok * kCntWords);
     int* red = reinterpret_cast<int*>(smem + kOffRed) + w * 4;
     uint8_t* qs = smem + kOffQ + w * kQBytes;
     const uint32_t bar_id = 1 + w;
     const IdxT* idx = static_cast<const IdxT*>(p.idx);
-    // counters of whole 128-key chunks (the last chunk may run past n_kv)
-    const int nkv_words = ((p.nkv + kChunk - 1) / kChunk) * (kChunk / 2);
+    // counters of whole chunks (the last chunk may run past n_kv)
+    const int nkv_words = ((p.nkv + kChunk - 1) / kChunk) * kChunk;
     bool ok = true;
     int li = 0, g = 0;
     for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++li) {
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- counts of this tile's tokens and the number of chunks to visit
       int maxidx = -1;
       if (valid) {
-        for (int i = t * 4; i < p.tpt * nkv_words; i += 128 * 4)  // nkv_words % 32 == 0
+        for (int i = t * 4; i < p.tpt * nkv_words; i += 128 * 4)  // nkv_words % 64 == 0
           *reinterpret_cast<uint4*>(&cnt[(i / nkv_words) * kCntWords + (i % nkv_words)]) =
               make_uint4(0, 0, 0, 0);
         named_bar_sync(bar_id, 128);
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (k >= 0 && k < p.nkv) {
               const int i = i0 + u * 128 + t;
               const int kk = static_cast<int>(k);
-              atomicAdd(&cnt[(i / p.topk) * kCntWords + (kk >> 1)], 1u << ((kk & 1) * 16));
+              atomicAdd(&cnt[(i / p.topk) * kCntWords + kk], 1u);
               maxidx = max(maxidx, kk);
             }
           }
@@ -366,6 +366,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(bar_id, 128);
       const int mx_all = max(max(red[0], red[1]), max(red[2], red[3]));
       const int nc = valid ? (mx_all + kChunk) / kChunk : 0;  // chunks holding any counted row
+      // count c -> log2(c) (-inf for 0): the softmax weight c e^s becomes 2^(s log2e + log2 c)
+      if (nc > 0) {
+        const int nw = nc * kChunk;
+        for (int i = t * 4; i < p.tpt * nw; i += 128 * 4) {
+          uint4* a = reinterpret_cast<uint4*>(&cnt[(i / nw) * kCntWords + (i % nw)]);
+          uint4 v = *a;
+          v.x = v.x ? __float_as_uint(log2f(static_cast<float>(v.x))) : 0xFF800000u;
+          v.y = v.y ? __float_as_uint(log2f(static_cast<float>(v.y))) : 0xFF800000u;
+          v.z = v.z ? __float_as_uint(log2f(static_cast<float>(v.z))) : 0xFF800000u;
+          v.w = v.w ? __float_as_uint(log2f(static_cast<float>(v.w))) : 0xFF800000u;
+          *a = v;
+        }
+        named_bar_sync(bar_id, 128);
+      }
       if (t == 0) {
         meta[w] = nc;
         mbar_arrive(&meta_full[w]);
@@ -381,24 +395,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t sp = sp0 + static_cast<uint32_t>(j * kChunk);
-        const uint32_t* cw = my_cnt + c * (kChunk / 2);
+        const float* cb = my_bias + c * kChunk;
         // the chunk's 64 scores in registers, one read of S
         uint32_t sv[kChunk];
         tmem_ld_32x32b_x32(sp, *reinterpret_cast<uint32_t(*)[32]>(sv));
         tmem_ld_32x32b_x32(sp + 32u, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        // counts: 16 bits per key, read from shared memory (a broadcast) per 8 keys
+        // z = s scale log2e + log2 c (a shared-memory broadcast per 4 keys); -inf if c = 0
         float mx = -INFINITY;
 #pragma unroll
-        for (int q4 = 0; q4 < kChunk / 8; ++q4) {
-          const uint4 v = reinterpret_cast<const uint4*>(cw)[q4];
-          const uint32_t cv[4] = {v.x, v.y, v.z, v.w};
+        for (int q4 = 0; q4 < kChunk / 4; ++q4) {
+          const float4 bv = reinterpret_cast<const float4*>(cb)[q4];
+          const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            if ((cv[k >> 1] >> ((k & 1) * 16)) & 0xFFFFu)
-              mx = fmaxf(mx, __uint_as_float(sv[8 * q4 + k]));
+          for (int k = 0; k < 4; ++k) {
+            const float z = fmaf(__uint_as_float(sv[4 * q4 + k]), p.scale_log2, bb[k]);
+            sv[4 * q4 + k] = __float_as_uint(z);
+            mx = fmaxf(mx, z);
           }
         }
-        mx *= p.scale_log2;  // scale > 0: the max of the scaled scores
         // running max; O is rescaled only when the max grows by more than 2^8
         float factor = 1.f;
         if (c == 0) {
@@ -424,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
           }
         }
-        // P = c_k 2^(z - m) as bf16 hi + lo over the S columns of the same keys:
+        // P = 2^(z - m) = c_k 2^(s' - m) as bf16 hi + lo over the S columns of the same keys:
         // keys [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in [32h+16, 32h+32)
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -432,16 +446,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[32];
 #pragma unroll
           for (int k2 = 0; k2 < 16; ++k2) {
-            const uint32_t cword = cw[hh * 16 + k2];
             float e[2];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int k = hh * 32 + 2 * k2 + u;
-              const uint32_t ck = (cword >> (u * 16)) & 0xFFFFu;
-              const float z = fmaf(__uint_as_float(sv[k]), p.scale_log2, -m_run);
-              // exact float of the count (< 2^23) without a conversion instruction
-              const float ckf = __uint_as_float(0x4B000000u | ck) - 8388608.0f;
-              e[u] = ck ? ckf * ex2_approx(z) : 0.f;
+              e[u] = ex2_approx(__uint_as_float(sv[k]) - m_run);  // 2^-inf = 0
               ls[(k2 & 1) * 2 + u] += e[u];
             }
             const uint32_t hi = pack_bf16x2(e[0], e[1]);
