@@ -14,17 +14,24 @@
 // B200 mapping. A tile is 128 (token, head) rows (2 tokens of 64 heads, or 1 of
 // 128); a work item is two consecutive tiles of one batch, one per softmax
 // warpgroup, which share every kv chunk. Per CTA (one per SM, persistent):
-//   warp 0      TMA: the two q tiles, then kv chunks into a 3-stage ring.
+//   warp 0      TMA: kv chunks into a 4-stage ring (the first chunks of an item
+//               before its q tiles, so they arrive during the previous
+//               item's epilogue), the two q tiles.
 //   warp 1      tcgen05 issuer, per chunk and tile:
 //                 S[128 x 64]  = Q . KV_c^T              (8 x K16, smem operands)
 //                 O[128 x 128] += (P_hi + P_lo) . KV_c   (8 x K16, P read from TMEM)
+//               and releases a q tile as soon as its last S product completed.
 //   warps 2..9  two softmax warpgroups (tile 0 / tile 1 of the item). A thread
-//               owns one row: it builds the tile's per-token counts c_k in
-//               shared memory, then per chunk reads S, keeps a running max
-//               (O in TMEM is rescaled only when the max grows by more than
-//               2^8), writes P = c_k 2^(z - m) back over S as two bf16 pieces
-//               (P_hi + P_lo carries ~16 bits), and after the last chunk
-//               divides O by the running sum plus the sink term and stores.
+//               owns one row. Per item the warpgroup turns the tile's counts
+//               into log2(c_k) per key; per chunk a thread reads S once, keeps
+//               a running max (O in TMEM is rescaled only when the max grows by
+//               more than 2^8), writes P = c_k 2^(z - m) back over S as two
+//               bf16 pieces (P_hi + P_lo carries ~16 bits), and after the last
+//               chunk divides O by the running sum plus the sink term and
+//               stores through the (then free) log2-count buffer.
+//   warps 10,11 count builders: the counts c_k of the NEXT item's tokens
+//               (shared-memory atomics on 16-bit counters) and its chunk
+//               count, while the current item computes.
 // Chunks are 64 kv rows. TMEM per warpgroup w: two S/P buffers at columns
 // [256w, 256w+64) and [256w+64, 256w+128), O at [256w+128, 256w+256). An S/P
 // buffer is reused two chunks later, once that chunk's PV product completed
@@ -41,22 +48,22 @@ constexpr int kD = 128;
 constexpr int kChunk = 64;
 constexpr int kMaxNkv = 4096;
 constexpr int kKVStages = 4;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kQBytes = kRows * kD * 2;           // 32768
 constexpr int kQBoxBytes = kRows * 64 * 2;        // 16384
 constexpr int kKVBytes = kChunk * kD * 2;         // 16384
 constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 8192
-constexpr int kCntWords = kMaxNkv;                // a count, then log2(count), per key
 constexpr int kOffQ = 0;                                        // [2 wg]
 constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
-constexpr int kOffCnt = kOffKV + kKVStages * kKVBytes;          // 131072: [2 wg][2 tok]
-constexpr int kOffMeta = kOffCnt + 2 * 2 * kCntWords * 4;       // 196608
-constexpr int kOffRed = kOffMeta + 64;                          // [2 wg][4 warps] max index
-constexpr int kOffBar = kOffRed + 64;
-constexpr int kNumBars = 2 * 3 + 2 * kKVStages + 2 * 2 * 3 + 2 + 1;
+constexpr int kOffBias = kOffKV + kKVStages * kKVBytes;         // 131072: [2 wg][2 tok][n] f32
+constexpr int kOffCnt = kOffBias + 2 * 2 * kMaxNkv * 4;         // 196608: [2 wg][2 tok][n] u16
+constexpr int kOffMeta = kOffCnt + 2 * 2 * kMaxNkv * 2;         // 229376
+constexpr int kOffBar = kOffMeta + 64;
+constexpr int kNumBars = 2 + 2 + 4 + 2 + 2 + 2 * kKVStages + 4 * 3 + 2 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
+static_assert(kRows * kD * 2 == 2 * kMaxNkv * 4, "output staging reuses a log2-count buffer");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // O is rescaled when the max grows by more than 2^8
 
@@ -83,10 +90,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars;                       // [2] TMA -> MMA / softmax
-  uint64_t* q_empty = bars + 2;                  // [2] output stored -> producer
-  uint64_t* meta_full = bars + 4;                // [2] counts and chunk count ready
-  uint64_t* kv_full = bars + 6;                  // [kKVStages]
+  uint64_t* q_full = bars;                       // [2] TMA -> MMA
+  uint64_t* q_empty = bars + 2;                  // [2] last S product of the tile done -> TMA
+  uint64_t* meta_full = bars + 4;                // [2 wg][2 slot] counts and chunk count ready
+  uint64_t* cnt_empty = bars + 8;                // [2] counts turned into log2 -> count warps
+  uint64_t* meta_empty = bars + 10;              // [2 slot] chunk counts read by TMA and MMA
+  uint64_t* kv_full = bars + 12;                 // [kKVStages]
   uint64_t* kv_empty = kv_full + kKVStages;      // [kKVStages]
   // per warpgroup w and S buffer j: index [2 w + j]
   uint64_t* s_full = kv_empty + kKVStages;       // [4] S of a chunk in TMEM
@@ -96,7 +105,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain_bar = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
-  volatile int* meta = reinterpret_cast<volatile int*>(smem + kOffMeta);  // [2] chunks per tile
+  // meta[2 w + slot]: chunks of tile w of the item in slot (li & 1); red: count-warp maxima
+  volatile int* meta = reinterpret_cast<volatile int*>(smem + kOffMeta);
+  volatile int* red = meta + 4;
+  uint32_t* cnt32 = reinterpret_cast<uint32_t*>(smem + kOffCnt);  // two 16-bit counters a word
+  float* bias = reinterpret_cast<float*>(smem + kOffBias);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -105,7 +118,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; w < 2; ++w) {
       mbar_init(&q_full[w], 1);
       mbar_init(&q_empty[w], 1);
-      mbar_init(&meta_full[w], 1);
+      mbar_init(&meta_full[2 * w], 1);
+      mbar_init(&meta_full[2 * w + 1], 1);
+      mbar_init(&cnt_empty[w], 1);
+      mbar_init(&meta_empty[w], 2);
       mbar_init(&o_empty[w], 128);
     }
     for (int i = 0; i < 4; ++i) {
@@ -146,11 +162,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int li = 0, gc = 0;
       bool ok = true;
+      auto load_kv = [&](int b, int c) -> bool {
+        const int s = gc % kKVStages;
+        if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
+                       DSA_DEVERR_SA_WAIT))
+          return false;
+        uint8_t* kvs = smem + kOffKV + s * kKVBytes;
+        mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+        tma_load_3d(kvs, &tm_kv, 0, c * kChunk, b, &kv_full[s]);
+        tma_load_3d(kvs + kKVBoxBytes, &tm_kv, 64, c * kChunk, b, &kv_full[s]);
+        ++gc;
+        return true;
+      };
       for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
+        int nc = 0;
+        for (int w = 0; w < 2; ++w) {
+          if (!mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT)) {
+            ok = false;
+            break;
+          }
+          nc = max(nc, static_cast<int>(meta[2 * w + (li & 1)]));
+        }
+        if (!ok) break;
+        mbar_arrive(&meta_empty[li & 1]);
+        const int b = static_cast<int>(item / p.items_per_batch);
+        // the first kKVStages chunks reuse stages that earlier items' products free
+        const int npre = min(nc, kKVStages);
+        for (int c = 0; c < npre && ok; ++c) ok = load_kv(b, c);
         for (int w = 0; w < 2 && ok; ++w) {
-          int b, tb;
+          int bb, tb;
           bool valid;
-          tile_of(item, w, b, tb, valid);
+          tile_of(item, w, bb, tb, valid);
           if (!mbar_wait(&q_empty[w], (li & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
             ok = false;
             break;
@@ -164,29 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&q_full[w]);
           }
         }
-        if (!ok) break;
-        int nc = 0;
-        for (int w = 0; w < 2; ++w) {
-          if (!mbar_wait(&meta_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
-            ok = false;
-            break;
-          }
-          nc = max(nc, static_cast<int>(meta[w]));
-        }
-        if (!ok) break;
-        const int b = static_cast<int>(item / p.items_per_batch);
-        for (int c = 0; c < nc; ++c, ++gc) {
-          const int s = gc % kKVStages;
-          if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
-                         DSA_DEVERR_SA_WAIT)) {
-            ok = false;
-            break;
-          }
-          uint8_t* kvs = smem + kOffKV + s * kKVBytes;
-          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
-          tma_load_3d(kvs, &tm_kv, 0, c * kChunk, b, &kv_full[s]);
-          tma_load_3d(kvs + kKVBoxBytes, &tm_kv, 64, c * kChunk, b, &kv_full[s]);
-        }
+        for (int c = npre; c < nc && ok; ++c) ok = load_kv(b, c);
       }
       for (int i = (gc > kKVStages ? gc - kKVStages : 0); i < gc; ++i)
         mbar_drain(&kv_full[i % kKVStages], (i / kKVStages) & 1);
@@ -209,14 +230,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
         int ncw[2];
         for (int w = 0; w < 2 && ok; ++w) {
-          if (!mbar_wait(&q_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT) ||
-              !mbar_wait(&meta_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
+          if (!mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT) ||
+              !mbar_wait(&q_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
             ok = false;
             break;
           }
-          ncw[w] = meta[w];
+          ncw[w] = meta[2 * w + (li & 1)];
+          if (ncw[w] == 0) umma_commit(&q_empty[w]);
         }
         if (!ok) break;
+        mbar_arrive(&meta_empty[li & 1]);
         const int nc = max(ncw[0], ncw[1]);
         uint32_t prev_kvb = 0;
         int prev_s = 0;
@@ -254,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
               }
               umma_commit(&s_full[2 * w + j]);
+              if (c == ncw[w] - 1) umma_commit(&q_empty[w]);  // q tile no longer read
               ++gs[w];
             }
             if (!ok) break;
@@ -305,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(drain_bar);
       mbar_drain(drain_bar, 0);
     }
-  } else {
+  } else if (warp < 10) {
     // ------------------------------------------------------------ softmax warpgroups
     const int w = (warp - 2) >> 2;
     const int t = threadIdx.x - 64 - 128 * w;   // 0..127
@@ -317,75 +342,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sp0 = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P buffers
     const uint32_t od = sp0 + 2u * kChunk;                                    // O
     const float sink2 = p.sink[h] * kLog2e;
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt) + w * 2 * kCntWords;
-    const float* my_bias = reinterpret_cast<const float*>(cnt + tok * kCntWords);
-    int* red = reinterpret_cast<int*>(smem + kOffRed) + w * 4;
-    uint8_t* qs = smem + kOffQ + w * kQBytes;
+    float* wbias = bias + w * 2 * kMaxNkv;                 // this warpgroup's [2 tok][n]
+    const float* my_bias = wbias + tok * kMaxNkv;
+    uint32_t* wcnt = cnt32 + w * kMaxNkv;                  // [2 tok][n / 2] words
+    uint8_t* stage = reinterpret_cast<uint8_t*>(wbias);    // output staging after the chunks
     const uint32_t bar_id = 1 + w;
-    const IdxT* idx = static_cast<const IdxT*>(p.idx);
-    // counters of whole chunks (the last chunk may run past n_kv)
-    const int nkv_words = ((p.nkv + kChunk - 1) / kChunk) * kChunk;
     bool ok = true;
     int li = 0, g = 0;
     for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++li) {
       int b, tb;
       bool valid;
       tile_of(item, w, b, tb, valid);
-      // ---- counts of this tile's tokens and the number of chunks to visit
-      int maxidx = -1;
-      if (valid) {
-        for (int i = t * 4; i < p.tpt * nkv_words; i += 128 * 4)  // nkv_words % 64 == 0
-          *reinterpret_cast<uint4*>(&cnt[(i / nkv_words) * kCntWords + (i % nkv_words)]) =
-              make_uint4(0, 0, 0, 0);
-        named_bar_sync(bar_id, 128);
-        const int64_t tok0 = static_cast<int64_t>(tb) * kRows / p.heads;
-        const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
-        const int n_ent = p.tpt * p.topk;
-        // batches of 8 independent loads ahead of their shared-memory atomics
-        for (int i0 = 0; i0 < n_ent; i0 += 8 * 128) {
-          int64_t kb[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * 128 + t;
-            kb[u] = i < n_ent ? static_cast<int64_t>(__ldg(src + i)) : -1;
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int64_t k = kb[u];
-            if (k >= 0 && k < p.nkv) {
-              const int i = i0 + u * 128 + t;
-              const int kk = static_cast<int>(k);
-              atomicAdd(&cnt[(i / p.topk) * kCntWords + kk], 1u);
-              maxidx = max(maxidx, kk);
-            }
-          }
-        }
-      }
-      maxidx = __reduce_max_sync(0xFFFFFFFFu, maxidx);
-      if (lane == 0) red[quarter] = maxidx;
-      named_bar_sync(bar_id, 128);
-      const int mx_all = max(max(red[0], red[1]), max(red[2], red[3]));
-      const int nc = valid ? (mx_all + kChunk) / kChunk : 0;  // chunks holding any counted row
-      // count c -> log2(c) (-inf for 0): the softmax weight c e^s becomes 2^(s log2e + log2 c)
+      // the previous item's output has left the staging buffer
+      if (t == 0) bulk_wait_group_read<0>();
+      const bool okm = mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
+                                 DSA_DEVERR_SA_WAIT);
+      ok = named_bar_and(bar_id, 128, okm);
+      if (!ok) break;
+      const int nc = meta[2 * w + (li & 1)];
+      // ---- counts -> log2(c) per key (-inf for c = 0), zeroing the counters;
+      // the softmax weight c e^s becomes 2^(s log2e + log2 c)
       if (nc > 0) {
-        const int nw = nc * kChunk;
-        for (int i = t * 4; i < p.tpt * nw; i += 128 * 4) {
-          uint4* a = reinterpret_cast<uint4*>(&cnt[(i / nw) * kCntWords + (i % nw)]);
-          uint4 v = *a;
-          v.x = v.x ? __float_as_uint(log2f(static_cast<float>(v.x))) : 0xFF800000u;
-          v.y = v.y ? __float_as_uint(log2f(static_cast<float>(v.y))) : 0xFF800000u;
-          v.z = v.z ? __float_as_uint(log2f(static_cast<float>(v.z))) : 0xFF800000u;
-          v.w = v.w ? __float_as_uint(log2f(static_cast<float>(v.w))) : 0xFF800000u;
-          *a = v;
+        const int n8 = nc * (kChunk / 8);  // 8-key groups per token
+        for (int i = t; i < p.tpt * n8; i += 128) {
+          const int tk = i / n8, q8 = i - tk * n8;
+          uint4* cp = reinterpret_cast<uint4*>(wcnt + tk * (kMaxNkv / 2)) + q8;
+          const uint4 v = *cp;
+          *cp = make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+          float f[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t c = (wd[u >> 1] >> ((u & 1) * 16)) & 0xFFFFu;
+            f[u] = c ? 0.f : -INFINITY;
+            if (c > 1) f[u] = log2f(static_cast<float>(c));
+          }
+          float4* bp = reinterpret_cast<float4*>(wbias + tk * kMaxNkv) + q8 * 2;
+          bp[0] = make_float4(f[0], f[1], f[2], f[3]);
+          bp[1] = make_float4(f[4], f[5], f[6], f[7]);
         }
-        named_bar_sync(bar_id, 128);
       }
-      if (t == 0) {
-        meta[w] = nc;
-        mbar_arrive(&meta_full[w]);
-      }
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&q_full[w], li & 1, abort_flag, p.err,
-                                             DSA_DEVERR_SA_WAIT));
+      named_bar_sync(bar_id, 128);
+      if (t == 0) mbar_arrive(&cnt_empty[w]);
       // ---- chunks
       float m_run = sink2, l_run = 0.f;
       for (int c = 0; ok && c < nc; ++c, ++g) {
@@ -465,7 +463,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&p_full[2 * w + j]);
       }
-      // ---- epilogue: O / (l + sink term) -> bf16 -> q buffer (SW128) -> TMA store
+      // ---- epilogue: O / (l + sink term) -> bf16 -> staging (SW128) -> TMA store.
+      // Every thread's log2-count reads precede its P of the last chunk, so once
+      // that chunk's product completed the buffer is free for staging.
       if (ok && nc > 0) {
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[2 * w + ((g - 1) & 1)], ((g - 1) >> 1) & 1,
                                                abort_flag, p.err, DSA_DEVERR_SA_WAIT));
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && valid) {
         const float inv = 1.0f / (l_run + ex2_approx(sink2 - m_run));
         if (nc > 0) tc_fence_after();
-        const uint32_t ob_row = smem_u32(qs) + static_cast<uint32_t>(row) * 128u;
+        const uint32_t ob_row = smem_u32(stage) + static_cast<uint32_t>(row) * 128u;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t ov[32];
@@ -503,17 +503,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
       }
       if (!named_bar_and(bar_id, 128, ok)) break;
-      if (t == 0) {
-        if (valid) {
-          tma_store_3d(&tm_out, qs, 0, tb * kRows, b);
-          tma_store_3d(&tm_out, qs + kQBoxBytes, 64, tb * kRows, b);
-          bulk_commit_group();
-          bulk_wait_group_read<0>();
-        }
-        mbar_arrive(&q_empty[w]);
+      if (t == 0 && valid) {
+        tma_store_3d(&tm_out, stage, 0, tb * kRows, b);
+        tma_store_3d(&tm_out, stage + kQBoxBytes, 64, tb * kRows, b);
+        bulk_commit_group();
       }
     }
     if (t == 0) bulk_wait_group<0>();
+  } else {
+    // ------------------------------------------------------------ count builders
+    // counts of item li go to the shared counters once both warpgroups turned
+    // item li-1's counts into log2 (and zeroed them); 16-bit counters, two per word
+    const int ct = threadIdx.x - 320;  // 0..63
+    const IdxT* idx = static_cast<const IdxT*>(p.idx);
+    for (int i = ct * 4; i < 2 * 2 * kMaxNkv / 2; i += 64 * 4)
+      *reinterpret_cast<uint4*>(&cnt32[i]) = make_uint4(0u, 0u, 0u, 0u);
+    named_bar_sync(3, 64);
+    int li = 0;
+    bool ok = true;
+    for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++li) {
+      bool okw = true;
+      for (int w = 0; w < 2; ++w)
+        okw = okw && mbar_wait(&cnt_empty[w], (li & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT);
+      ok = named_bar_and(3, 64, okw);
+      if (!ok) break;
+      for (int w = 0; w < 2; ++w) {
+        int b, tb;
+        bool valid;
+        tile_of(item, w, b, tb, valid);
+        int maxidx = -1;
+        if (valid) {
+          const int64_t tok0 = static_cast<int64_t>(tb) * kRows / p.heads;
+          const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
+          uint32_t* wcnt = cnt32 + w * kMaxNkv;
+          const int n_ent = p.tpt * p.topk;
+          // batches of 8 independent loads ahead of their shared-memory atomics
+          for (int i0 = 0; i0 < n_ent; i0 += 8 * 64) {
+            int64_t kb[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int i = i0 + u * 64 + ct;
+              kb[u] = i < n_ent ? static_cast<int64_t>(__ldg(src + i)) : -1;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int64_t k = kb[u];
+              if (k >= 0 && k < p.nkv) {
+                const int i = i0 + u * 64 + ct;
+                const int kk = static_cast<int>(k);
+                atomicAdd(&wcnt[(i / p.topk) * (kMaxNkv / 2) + (kk >> 1)], 1u << ((kk & 1) * 16));
+                maxidx = max(maxidx, kk);
+              }
+            }
+          }
+        }
+        maxidx = __reduce_max_sync(0xFFFFFFFFu, maxidx);
+        if (lane == 0) red[2 * (warp - 10) + w] = maxidx;
+      }
+      // the TMA and MMA warps have read this slot's chunk counts of item li-2
+      const bool okm = mbar_wait(&meta_empty[li & 1], ((li >> 1) & 1) ^ 1, abort_flag, p.err,
+                                 DSA_DEVERR_SA_WAIT);
+      ok = named_bar_and(3, 64, okm);
+      if (!ok) break;
+      if (ct == 0) {
+        for (int w = 0; w < 2; ++w) {
+          int b, tb;
+          bool valid;
+          tile_of(item, w, b, tb, valid);
+          const int mx = max(red[w], red[2 + w]);
+          meta[2 * w + (li & 1)] = valid ? (mx + kChunk) / kChunk : 0;  // chunks with a counted row
+          mbar_arrive(&meta_full[2 * w + (li & 1)]);
+        }
+      }
+    }
   }
 
   __syncwarp();
