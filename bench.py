@@ -43,13 +43,18 @@ METRIC = "sparse_attn tokens/s (µs/call in ms_per_step)"
 FALLBACK_HBM_GBS = 6650.0
 
 
-def load_peaks():
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def load_peaks(key="hbm_gbs"):
+    """Measured peak (HBM GB/s or burst bf16 TFLOP/s) and whether it is measured or fallback."""
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
-    return FALLBACK_HBM_GBS, "fallback"
+        if key in p:
+            return float(p[key]), "measured"
+    return (FALLBACK_HBM_GBS if key == "hbm_gbs" else FALLBACK_BF16_TFLOPS), "fallback"
 
 
 def load_traffic():
@@ -234,7 +239,77 @@ def bench_other_ops(dev):
                           "shape": "x[8,2600,1024] qr[8,2600,256] kv_cache[8,650,64] top-128"}
     except Exception as exc:  # reported, not hidden: the indexer line says why
         res["indexer"] = {"error": str(exc).splitlines()[0][:200]}
+    try:
+        res["chain"] = bench_chain(dev)
+    except Exception as exc:
+        res["chain"] = {"error": str(exc).splitlines()[0][:200]}
     return res
+
+
+def make_chain_case(dev, b):
+    """BASELINE configs[3] inputs at batch b: indexer ModelNew (top-2048 over a
+    [b,4096,64] compressed kv_cache), x, qr, and the attention q / kv pool / sink."""
+    import torch
+
+    from ascendc_kernel_b200 import indexer as ix
+
+    s_len, t_cache = 16384, 4096
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(42)
+    torch.manual_seed(42)
+    a = ix.ModelArgs(max_batch_size=b, max_seq_len=s_len, dim=1024, index_n_heads=16,
+                     index_head_dim=64, index_topk=2048, q_lora_rank=256, rope_head_dim=32)
+    kvc = torch.randn(b, t_cache, 64, dtype=torch.bfloat16, device=dev, generator=gen)
+    model = ix.ModelNew(a, ix.make_freqs_cis(32, s_len), kvc, 4).to(dev)
+    x = torch.randn(b, s_len, 1024, dtype=torch.bfloat16, device=dev, generator=gen)
+    qr = torch.randn(b, s_len, 256, dtype=torch.bfloat16, device=dev, generator=gen)
+    q = torch.randn(b, s_len, 64, 128, dtype=torch.bfloat16, device=dev, generator=gen)
+    pool = torch.randn(b, t_cache, 128, dtype=torch.bfloat16, device=dev, generator=gen)
+    sink = torch.zeros(64, dtype=torch.float32, device=dev)
+    return model, x, qr, q, pool, sink
+
+
+def bench_chain(dev):
+    """indexer top-2048 over kv_cache[4,4096,64] for x[4,16384,1024],
+    its int64 indices feeding SparseAttention of q[4,16384,64,128] over a kv pool
+    [4,4096,128]. Synthetic randn inputs from one seed; CUDA-event µs per call."""
+    import torch
+
+    from ascendc_kernel_b200 import sparse_attn as sa
+
+    b, s_len = 4, 16384
+    model, x, qr, q, pool, sink = make_chain_case(dev, b)
+    out = torch.empty_like(q)
+    scale = 128 ** -0.5
+
+    def timed(fn, n=5):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / n
+
+    idx = model(x, qr, 0, 0)
+    ix_us = timed(lambda: model(x, qr, 0, 0))
+    sa_us = timed(lambda: sa.sparse_attn(q, pool, sink, idx, scale, out=out))
+    chain_us = timed(lambda: sa.sparse_attn(q, pool, sink, model(x, qr, 0, 0), scale, out=out))
+    valid = int((idx >= 0).sum())
+    peak, peak_kind = load_peaks("bf16_tflops")
+    flops = valid * 64 * 128 * 4
+    sa_tflops = flops / (sa_us * 1e-6) / 1e12
+    return {"indexer_us": ix_us, "sparse_attn_us": sa_us, "chain_us": chain_us,
+            "tokens_per_s": b * s_len / (chain_us * 1e-6),
+            "valid_index_pairs": valid,
+            "sparse_attn_tflops": sa_tflops, "sparse_attn_frac_of_bf16_peak": sa_tflops / peak,
+            "bf16_peak_source": peak_kind,
+            "sparse_attn_algorithmic_flops": flops,
+            "shape": "x[4,16384,1024] qr[4,16384,256] kv_cache[4,4096,64] top-2048 -> "
+                     "q[4,16384,64,128] over kv pool [4,4096,128] (BASELINE configs[3])"}
 
 
 def run_ours(args, world, rank, local):
@@ -397,6 +472,17 @@ def run_profile_case(args):
         print(json.dumps({"profile_case": "ix", "batch": 8, "launches":
                           3 * (args.warmup + args.steps)}))
         return
+    if args.profile == "chain":
+        # configs[3] at batch args.batch (1: ~0.9 GB on the device): indexer top-2048,
+        # then the long-pool SparseAttention over its indices
+        model, x, qr, q, pool, sink = make_chain_case(dev, args.batch)
+        out = torch.empty_like(q)
+        for _ in range(args.warmup + args.steps):
+            sa.sparse_attn(q, pool, sink, model(x, qr, 0, 0), 128 ** -0.5, out=out)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "chain", "batch": args.batch,
+                          "steps": args.warmup + args.steps}))
+        return
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)
     b = args.batch
@@ -418,7 +504,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa", "ix"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix", "chain"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()
