@@ -192,6 +192,13 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
   return d;
 }
 
+// A 64-bit descriptor from its two 32-bit words (a register pair, no shifts).
+__device__ __forceinline__ uint64_t desc_from_words(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
 //   [4,6) D fmt (1 = f32)  [7,10) A fmt (1 = bf16)  [10,13) B fmt (1 = bf16)
 //   bit 15 A major (0 K, 1 MN)  bit 16 B major  [17,23) N>>3  [24,29) M>>4

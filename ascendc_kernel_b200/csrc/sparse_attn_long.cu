@@ -220,110 +220,111 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc1 = make_idesc_bf16_f32(128, kChunk, 0, 0);
       constexpr uint32_t idesc2 = make_idesc_bf16_f32(128, kD, 0, 1);
-      const uint32_t q_base = smem_u32(smem + kOffQ);
-      const uint32_t kv_base = smem_u32(smem + kOffKV);
+      // Descriptors are built once; per MMA only the 14-bit start-address field
+      // (low word, 16-byte units) moves, by compile-time offsets, so the single
+      // issuing thread spends a few instructions per MMA (every smem address
+      // here is below 256 KB, so the field never carries into the LBO bits).
+      const uint64_t dq = make_smem_desc(smem_u32(smem + kOffQ), 16u, 1024u, kLayoutSW128);
+      const uint64_t dkv = make_smem_desc(smem_u32(smem + kOffKV), 16u, 1024u, kLayoutSW128);
+      const uint32_t hi = static_cast<uint32_t>(dkv >> 32);  // SBO 1024, SW128: shared by all
+      const uint32_t q_lo = static_cast<uint32_t>(dq);
+      const uint32_t kvk_lo = static_cast<uint32_t>(dkv);  // K-major kv (S operand B)
+      const uint32_t kvmn_lo = static_cast<uint32_t>(      // MN-major kv (PV operand B)
+          make_smem_desc(smem_u32(smem + kOffKV), static_cast<uint32_t>(kKVBoxBytes), 1024u,
+                         kLayoutSW128));
       int li = 0, gc = 0;
       int gs[2] = {0, 0};     // S products issued per warpgroup (all items)
       int gm[2] = {0, 0};     // PV products issued per warpgroup
       int uses[2] = {0, 0};   // items per warpgroup that wrote O
+      int ncw[2] = {0, 0};
       bool ok = true;
+      // S of chunk c for warpgroup w from kv stage s (K-major operands)
+      auto issue_s = [&](int w, int c, int s) -> bool {
+        if (c >= ncw[w]) return true;
+        const int j = gs[w] & 1;
+        if (gs[w] >= 2 && !mbar_wait(&o_done[2 * w + j], ((gs[w] >> 1) + 1) & 1, abort_flag,
+                                     p.err, DSA_DEVERR_SA_WAIT))
+          return false;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
+        const uint32_t qa = q_lo + static_cast<uint32_t>(w * (kQBytes >> 4));
+        const uint32_t kb = kvk_lo + static_cast<uint32_t>(s * (kKVBytes >> 4));
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t ao = static_cast<uint32_t>(((k >> 2) * kQBoxBytes + (k & 3) * 32) >> 4);
+          const uint32_t bo = static_cast<uint32_t>(((k >> 2) * kKVBoxBytes + (k & 3) * 32) >> 4);
+          umma_bf16(d, desc_from_words(qa + ao, hi), desc_from_words(kb + bo, hi), idesc1,
+                    k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[2 * w + j]);
+        if (c == ncw[w] - 1) umma_commit(&q_empty[w]);  // q tile no longer read
+        ++gs[w];
+        return true;
+      };
+      // PV of chunk cp for warpgroup w from kv stage s (P in TMEM, MN-major kv)
+      auto issue_pv = [&](int w, int cp, int s) -> bool {
+        if (cp >= ncw[w]) return true;
+        const int j = gm[w] & 1;
+        if (!mbar_wait(&p_full[2 * w + j], (gm[w] >> 1) & 1, abort_flag, p.err,
+                       DSA_DEVERR_SA_WAIT))
+          return false;
+        if (cp == 0) {
+          if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
+                                        DSA_DEVERR_SA_WAIT))
+            return false;
+          ++uses[w];
+        }
+        tc_fence_after();
+        const uint32_t sp = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
+        const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + 2 * kChunk);
+        const uint32_t kb = kvmn_lo + static_cast<uint32_t>(s * (kKVBytes >> 4));
+#pragma unroll
+        for (int st = 0; st < kChunk / 16; ++st) {
+          // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
+          // dim atoms (64) one box apart, row atoms (8) 1024 B apart.
+          const uint64_t bd = desc_from_words(kb + static_cast<uint32_t>((st * 2048) >> 4), hi);
+          // A = P in TMEM: keys [32h, 32h+32) hold P_hi in columns [32h, 32h+16)
+          // and P_lo in [32h+16, 32h+32) (two bf16 per column)
+          const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
+          umma_bf16_tmem_a(d, a_hi, bd, idesc2, (cp > 0 || st > 0) ? 1u : 0u);
+          umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
+        }
+        umma_commit(&o_done[2 * w + j]);
+        ++gm[w];
+        return true;
+      };
       for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
-        int ncw[2];
-        for (int w = 0; w < 2 && ok; ++w) {
-          if (!mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
-                         DSA_DEVERR_SA_WAIT) ||
-              !mbar_wait(&q_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
-            ok = false;
-            break;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          ok = ok &&
+               mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT) &&
+               mbar_wait(&q_full[w], li & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT);
+          if (ok) {
+            ncw[w] = meta[2 * w + (li & 1)];
+            if (ncw[w] == 0) umma_commit(&q_empty[w]);
           }
-          ncw[w] = meta[2 * w + (li & 1)];
-          if (ncw[w] == 0) umma_commit(&q_empty[w]);
         }
         if (!ok) break;
         mbar_arrive(&meta_empty[li & 1]);
         const int nc = max(ncw[0], ncw[1]);
-        uint32_t prev_kvb = 0;
         int prev_s = 0;
         for (int c = 0; c <= nc && ok; ++c) {
-          uint32_t kvb = 0;
           int s = 0;
           if (c < nc) {
             s = gc % kKVStages;
-            if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
-                           DSA_DEVERR_SA_WAIT)) {
-              ok = false;
-              break;
-            }
+            ok = mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
+                           DSA_DEVERR_SA_WAIT);
+            if (!ok) break;
             ++gc;
-            kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
-            for (int w = 0; w < 2; ++w) {
-              if (c >= ncw[w]) continue;
-              const int j = gs[w] & 1;
-              if (gs[w] >= 2 && !mbar_wait(&o_done[2 * w + j], ((gs[w] >> 1) + 1) & 1, abort_flag,
-                                           p.err, DSA_DEVERR_SA_WAIT)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
-              const uint32_t qb = q_base + static_cast<uint32_t>(w) * kQBytes;
-#pragma unroll
-              for (int k = 0; k < kD / 16; ++k) {
-                const uint32_t box = static_cast<uint32_t>(k >> 2);
-                const uint32_t koff = static_cast<uint32_t>(k & 3) * 32u;
-                const uint64_t ad =
-                    make_smem_desc(qb + box * kQBoxBytes + koff, 16u, 1024u, kLayoutSW128);
-                const uint64_t bd =
-                    make_smem_desc(kvb + box * kKVBoxBytes + koff, 16u, 1024u, kLayoutSW128);
-                umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
-              }
-              umma_commit(&s_full[2 * w + j]);
-              if (c == ncw[w] - 1) umma_commit(&q_empty[w]);  // q tile no longer read
-              ++gs[w];
-            }
+            ok = issue_s(0, c, s) && issue_s(1, c, s);
             if (!ok) break;
           }
-          if (c >= 1) {
-            const int cp = c - 1;  // PV products of the previous chunk
-            for (int w = 0; w < 2; ++w) {
-              if (cp >= ncw[w]) continue;
-              const int j = gm[w] & 1;
-              if (!mbar_wait(&p_full[2 * w + j], (gm[w] >> 1) & 1, abort_flag, p.err,
-                             DSA_DEVERR_SA_WAIT)) {
-                ok = false;
-                break;
-              }
-              if (cp == 0) {
-                if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
-                                              DSA_DEVERR_SA_WAIT)) {
-                  ok = false;
-                  break;
-                }
-                ++uses[w];
-              }
-              tc_fence_after();
-              const uint32_t sp = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
-              const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + 2 * kChunk);
-#pragma unroll
-              for (int st = 0; st < kChunk / 16; ++st) {
-                // B = kv as [K = 16 kv rows] x [N = 128 dims], MN-major SW128:
-                // dim atoms (64) one box apart, row atoms (8) 1024 B apart.
-                const uint64_t bd = make_smem_desc(prev_kvb + static_cast<uint32_t>(st) * 2048u,
-                                                   static_cast<uint32_t>(kKVBoxBytes), 1024u,
-                                                   kLayoutSW128);
-                // A = P in TMEM: keys [32h, 32h+32) hold P_hi in columns [32h, 32h+16)
-                // and P_lo in [32h+16, 32h+32) (two bf16 per column)
-                const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
-                umma_bf16_tmem_a(d, a_hi, bd, idesc2, (cp > 0 || st > 0) ? 1u : 0u);
-                umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
-              }
-              umma_commit(&o_done[2 * w + j]);
-              ++gm[w];
-            }
+          if (c >= 1) {  // PV products of the previous chunk
+            ok = issue_pv(0, c - 1, prev_s) && issue_pv(1, c - 1, prev_s);
             if (!ok) break;
             umma_commit(&kv_empty[prev_s]);
           }
-          prev_kvb = kvb;
           prev_s = s;
         }
       }
