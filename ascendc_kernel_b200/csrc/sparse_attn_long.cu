@@ -45,22 +45,22 @@ namespace sal {
 
 constexpr int kRows = 128;
 constexpr int kD = 128;
-constexpr int kChunk = 64;
+constexpr int kChunk = 128;
 constexpr int kMaxNkv = 4096;
-constexpr int kKVStages = 4;
+constexpr int kKVStages = 2;
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kQBytes = kRows * kD * 2;           // 32768
 constexpr int kQBoxBytes = kRows * 64 * 2;        // 16384
-constexpr int kKVBytes = kChunk * kD * 2;         // 16384
-constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 8192
+constexpr int kKVBytes = kChunk * kD * 2;         // 32768
+constexpr int kKVBoxBytes = kChunk * 64 * 2;      // 16384
 constexpr int kOffQ = 0;                                        // [2 wg]
 constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
 constexpr int kOffBias = kOffKV + kKVStages * kKVBytes;         // 131072: [2 wg][2 tok][n] f32
 constexpr int kOffCnt = kOffBias + 2 * 2 * kMaxNkv * 4;         // 196608: [2 wg][2 tok][n] u16
 constexpr int kOffMeta = kOffCnt + 2 * 2 * kMaxNkv * 2;         // 229376
 constexpr int kOffBar = kOffMeta + 64;
-constexpr int kNumBars = 2 + 2 + 4 + 2 + 2 + 2 * kKVStages + 4 * 3 + 2 + 1;
+constexpr int kNumBars = 2 + 2 + 4 + 2 + 2 + 2 * kKVStages + 2 * 3 + 2 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kRows * kD * 2 == 2 * kMaxNkv * 4, "output staging reuses a log2-count buffer");
@@ -97,11 +97,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* meta_empty = bars + 10;              // [2 slot] chunk counts read by TMA and MMA
   uint64_t* kv_full = bars + 12;                 // [kKVStages]
   uint64_t* kv_empty = kv_full + kKVStages;      // [kKVStages]
-  // per warpgroup w and S buffer j: index [2 w + j]
-  uint64_t* s_full = kv_empty + kKVStages;       // [4] S of a chunk in TMEM
-  uint64_t* p_full = s_full + 4;                 // [4] P written (128 arrivals)
-  uint64_t* o_done = p_full + 4;                 // [4] PV product of the buffer's chunk done
-  uint64_t* o_empty = o_done + 4;                // [2] O read by the epilogue (128 arrivals)
+  uint64_t* s_full = kv_empty + kKVStages;       // [2] S of a chunk in TMEM
+  uint64_t* p_full = s_full + 2;                 // [2] P written (128 arrivals)
+  uint64_t* o_done = p_full + 2;                 // [2] PV product of a chunk completed
+  uint64_t* o_empty = o_done + 2;                // [2] O read by the epilogue (128 arrivals)
   uint64_t* drain_bar = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
@@ -124,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&meta_empty[w], 2);
       mbar_init(&o_empty[w], 128);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
@@ -238,15 +237,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int uses[2] = {0, 0};   // items per warpgroup that wrote O
       int ncw[2] = {0, 0};
       bool ok = true;
-      // S of chunk c for warpgroup w from kv stage s (K-major operands)
+      // S of chunk c for warpgroup w from kv stage s (K-major operands); the S/P
+      // columns are free once the previous chunk's PV product completed
       auto issue_s = [&](int w, int c, int s) -> bool {
         if (c >= ncw[w]) return true;
-        const int j = gs[w] & 1;
-        if (gs[w] >= 2 && !mbar_wait(&o_done[2 * w + j], ((gs[w] >> 1) + 1) & 1, abort_flag,
-                                     p.err, DSA_DEVERR_SA_WAIT))
+        if (gs[w] >= 1 && !mbar_wait(&o_done[w], (gs[w] - 1) & 1, abort_flag, p.err,
+                                     DSA_DEVERR_SA_WAIT))
           return false;
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
+        const uint32_t d = tmem + static_cast<uint32_t>(w * 256);
         const uint32_t qa = q_lo + static_cast<uint32_t>(w * (kQBytes >> 4));
         const uint32_t kb = kvk_lo + static_cast<uint32_t>(s * (kKVBytes >> 4));
 #pragma unroll
@@ -256,27 +255,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16(d, desc_from_words(qa + ao, hi), desc_from_words(kb + bo, hi), idesc1,
                     k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[2 * w + j]);
+        umma_commit(&s_full[w]);
         if (c == ncw[w] - 1) umma_commit(&q_empty[w]);  // q tile no longer read
         ++gs[w];
         return true;
       };
-      // PV of chunk cp for warpgroup w from kv stage s (P in TMEM, MN-major kv)
-      auto issue_pv = [&](int w, int cp, int s) -> bool {
-        if (cp >= ncw[w]) return true;
-        const int j = gm[w] & 1;
-        if (!mbar_wait(&p_full[2 * w + j], (gm[w] >> 1) & 1, abort_flag, p.err,
-                       DSA_DEVERR_SA_WAIT))
+      // PV of chunk c for warpgroup w from kv stage s (P in TMEM, MN-major kv)
+      auto issue_pv = [&](int w, int c, int s) -> bool {
+        if (c >= ncw[w]) return true;
+        if (!mbar_wait(&p_full[w], gm[w] & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT))
           return false;
-        if (cp == 0) {
+        if (c == 0) {
           if (uses[w] > 0 && !mbar_wait(&o_empty[w], (uses[w] - 1) & 1, abort_flag, p.err,
                                         DSA_DEVERR_SA_WAIT))
             return false;
           ++uses[w];
         }
         tc_fence_after();
-        const uint32_t sp = tmem + static_cast<uint32_t>(w * 256 + j * kChunk);
-        const uint32_t d = tmem + static_cast<uint32_t>(w * 256 + 2 * kChunk);
+        const uint32_t sp = tmem + static_cast<uint32_t>(w * 256);
+        const uint32_t d = sp + static_cast<uint32_t>(kChunk);
         const uint32_t kb = kvmn_lo + static_cast<uint32_t>(s * (kKVBytes >> 4));
 #pragma unroll
         for (int st = 0; st < kChunk / 16; ++st) {
@@ -286,12 +283,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // A = P in TMEM: keys [32h, 32h+32) hold P_hi in columns [32h, 32h+16)
           // and P_lo in [32h+16, 32h+32) (two bf16 per column)
           const uint32_t a_hi = sp + static_cast<uint32_t>((st >> 1) * 32 + (st & 1) * 8);
-          umma_bf16_tmem_a(d, a_hi, bd, idesc2, (cp > 0 || st > 0) ? 1u : 0u);
+          umma_bf16_tmem_a(d, a_hi, bd, idesc2, (c > 0 || st > 0) ? 1u : 0u);
           umma_bf16_tmem_a(d, a_hi + 16u, bd, idesc2, 1u);
         }
-        umma_commit(&o_done[2 * w + j]);
+        umma_commit(&o_done[w]);
         ++gm[w];
         return true;
+      };
+      auto wait_kv = [&](int i) -> bool {  // i: global chunk number
+        return mbar_wait(&kv_full[i % kKVStages], (i / kKVStages) & 1, abort_flag, p.err,
+                         DSA_DEVERR_SA_WAIT);
       };
       for (int64_t item = blockIdx.x; ok && item < p.total_items; item += gridDim.x, ++li) {
 #pragma unroll
@@ -308,25 +309,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mbar_arrive(&meta_empty[li & 1]);
         const int nc = max(ncw[0], ncw[1]);
-        int prev_s = 0;
-        for (int c = 0; c <= nc && ok; ++c) {
-          int s = 0;
-          if (c < nc) {
-            s = gc % kKVStages;
-            ok = mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
-                           DSA_DEVERR_SA_WAIT);
-            if (!ok) break;
-            ++gc;
-            ok = issue_s(0, c, s) && issue_s(1, c, s);
-            if (!ok) break;
-          }
-          if (c >= 1) {  // PV products of the previous chunk
-            ok = issue_pv(0, c - 1, prev_s) && issue_pv(1, c - 1, prev_s);
-            if (!ok) break;
-            umma_commit(&kv_empty[prev_s]);
-          }
-          prev_s = s;
+        // per chunk c: PV(c) of a tile, then S(c+1) of the same tile into the
+        // columns PV(c) just read, so one tile's S overlaps the other's softmax
+        if (nc > 0) {
+          ok = wait_kv(gc) && issue_s(0, 0, gc % kKVStages) && issue_s(1, 0, gc % kKVStages);
         }
+        for (int c = 0; c < nc && ok; ++c) {
+          const int s = (gc + c) % kKVStages;
+          const int sn = (gc + c + 1) % kKVStages;
+          const bool more = c + 1 < nc;
+          ok = issue_pv(0, c, s) && (!more || (wait_kv(gc + c + 1) && issue_s(0, c + 1, sn))) &&
+               issue_pv(1, c, s) && (!more || issue_s(1, c + 1, sn));
+          if (!ok) break;
+          umma_commit(&kv_empty[s]);
+        }
+        gc += nc;
       }
       umma_commit(drain_bar);
       mbar_drain(drain_bar, 0);
@@ -340,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tok = row / p.heads;
     const int h = row % p.heads;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t sp0 = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P buffers
-    const uint32_t od = sp0 + 2u * kChunk;                                    // O
+    const uint32_t sp = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P
+    const uint32_t od = sp + static_cast<uint32_t>(kChunk);                  // O
     const float sink2 = p.sink[h] * kLog2e;
     float* wbias = bias + w * 2 * kMaxNkv;                 // this warpgroup's [2 tok][n]
     const float* my_bias = wbias + tok * kMaxNkv;
@@ -388,28 +385,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- chunks
       float m_run = sink2, l_run = 0.f;
       for (int c = 0; ok && c < nc; ++c, ++g) {
-        const int j = g & 1;
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[2 * w + j], (g >> 1) & 1, abort_flag,
-                                               p.err, DSA_DEVERR_SA_WAIT));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], g & 1, abort_flag, p.err,
+                                               DSA_DEVERR_SA_WAIT));
         if (!ok) break;
         tc_fence_after();
-        const uint32_t sp = sp0 + static_cast<uint32_t>(j * kChunk);
         const float* cb = my_bias + c * kChunk;
-        // the chunk's 64 scores in registers, one read of S
-        uint32_t sv[kChunk];
-        tmem_ld_32x32b_x32(sp, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld_32x32b_x32(sp + 32u, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        // z = s scale log2e + log2 c (a shared-memory broadcast per 4 keys); -inf if c = 0
+        // pass 1: max over the chunk of z = s scale log2e + log2 c (-inf if c = 0);
+        // log2 c is a shared-memory broadcast per 4 keys
         float mx = -INFINITY;
+#pragma unroll 1
+        for (int q = 0; q < kChunk / 32; ++q) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q * 32), sv);
 #pragma unroll
-        for (int q4 = 0; q4 < kChunk / 4; ++q4) {
-          const float4 bv = reinterpret_cast<const float4*>(cb)[q4];
-          const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float z = fmaf(__uint_as_float(sv[4 * q4 + k]), p.scale_log2, bb[k]);
-            sv[4 * q4 + k] = __float_as_uint(z);
-            mx = fmaxf(mx, z);
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 bv = reinterpret_cast<const float4*>(cb + q * 32)[q4];
+            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 0]), p.scale_log2, bv.x));
+            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 1]), p.scale_log2, bv.y));
+            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 2]), p.scale_log2, bv.z));
+            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 3]), p.scale_log2, bv.w));
           }
         }
         // running max; O is rescaled only when the max grows by more than 2^8
@@ -422,13 +416,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           l_run *= factor;
         }
         if (c > 0 && __any_sync(0xFFFFFFFFu, factor != 1.f)) {
-          // O holds every earlier chunk's product once the last one completed
-          const int jp = (g - 1) & 1;
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[2 * w + jp], ((g - 1) >> 1) & 1,
-                                                 abort_flag, p.err, DSA_DEVERR_SA_WAIT));
+          // O holds every earlier chunk's product: this chunk's S was issued
+          // after the previous PV product completed
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
+                                                 DSA_DEVERR_SA_WAIT));
           if (!ok) break;
           tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int q4 = 0; q4 < 4; ++q4) {
             uint32_t ov[32];
             tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
@@ -437,39 +431,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
           }
         }
-        // P = 2^(z - m) = c_k 2^(s' - m) as bf16 hi + lo over the S columns of the same keys:
-        // keys [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in [32h+16, 32h+32)
+        // pass 2: P = 2^(z - m) = c_k 2^(s' - m) as bf16 hi + lo over the S columns of
+        // the same keys: keys [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in
+        // [32h+16, 32h+32); each group of 32 columns is read before it is written
+        const float negm = -m_run;
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+#pragma unroll 1
         for (int hh = 0; hh < kChunk / 32; ++hh) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(hh * 32), sv);
           uint32_t pk[32];
 #pragma unroll
-          for (int k2 = 0; k2 < 16; ++k2) {
-            float e[2];
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 bv = reinterpret_cast<const float4*>(cb + hh * 32)[q4];
+            const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
+            float e[4];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int k = hh * 32 + 2 * k2 + u;
-              e[u] = ex2_approx(__uint_as_float(sv[k]) - m_run);  // 2^-inf = 0
-              ls[(k2 & 1) * 2 + u] += e[u];
+            for (int u = 0; u < 4; ++u) {
+              e[u] = ex2_approx(fmaf(__uint_as_float(sv[4 * q4 + u]), p.scale_log2, bb[u]) + negm);
+              ls[u] += e[u];
             }
-            const uint32_t hi = pack_bf16x2(e[0], e[1]);
-            pk[k2] = hi;
-            pk[16 + k2] = pack_bf16x2(e[0] - bf16_bits_to_float(hi & 0xFFFFu),
-                                      e[1] - bf16_bits_to_float(hi >> 16));
+#pragma unroll
+            for (int u2 = 0; u2 < 2; ++u2) {
+              const uint32_t h2 = pack_bf16x2(e[2 * u2], e[2 * u2 + 1]);
+              pk[2 * q4 + u2] = h2;
+              pk[16 + 2 * q4 + u2] = pack_bf16x2(e[2 * u2] - bf16_bits_to_float(h2 & 0xFFFFu),
+                                                 e[2 * u2 + 1] - bf16_bits_to_float(h2 >> 16));
+            }
           }
           tmem_st_32x32b_x32_nowait(sp + static_cast<uint32_t>(hh * 32), pk);
         }
         l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[2 * w + j]);
+        mbar_arrive(&p_full[w]);
       }
       // ---- epilogue: O / (l + sink term) -> bf16 -> staging (SW128) -> TMA store.
       // Every thread's log2-count reads precede its P of the last chunk, so once
       // that chunk's product completed the buffer is free for staging.
       if (ok && nc > 0) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[2 * w + ((g - 1) & 1)], ((g - 1) >> 1) & 1,
-                                               abort_flag, p.err, DSA_DEVERR_SA_WAIT));
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
+                                               DSA_DEVERR_SA_WAIT));
       }
       if (ok && valid) {
         const float inv = 1.0f / (l_run + ex2_approx(sink2 - m_run));
