@@ -391,19 +391,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float* cb = my_bias + c * kChunk;
         // pass 1: max over the chunk of z = s scale log2e + log2 c (-inf if c = 0);
-        // log2 c is a shared-memory broadcast per 4 keys
+        // log2 c is a shared-memory broadcast per 4 keys. The next 32 columns load
+        // while the current 32 are reduced.
         float mx = -INFINITY;
-#pragma unroll 1
-        for (int q = 0; q < kChunk / 32; ++q) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(q * 32), sv);
+        {
+          uint32_t sa[32], sb[32];
+          auto reduce32 = [&](const uint32_t (&v)[32], int q) {
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4) {
-            const float4 bv = reinterpret_cast<const float4*>(cb + q * 32)[q4];
-            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 0]), p.scale_log2, bv.x));
-            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 1]), p.scale_log2, bv.y));
-            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 2]), p.scale_log2, bv.z));
-            mx = fmaxf(mx, fmaf(__uint_as_float(sv[4 * q4 + 3]), p.scale_log2, bv.w));
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 bv = reinterpret_cast<const float4*>(cb + q * 32)[q4];
+              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 0]), p.scale_log2, bv.x));
+              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 1]), p.scale_log2, bv.y));
+              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 2]), p.scale_log2, bv.z));
+              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 3]), p.scale_log2, bv.w));
+            }
+          };
+          tmem_ld_32x32b_x32_nowait(sp, sa);
+#pragma unroll 1
+          for (int q = 0; q < kChunk / 32; q += 2) {
+            tmem_wait_ld_dep(sa);
+            tmem_ld_32x32b_x32_nowait(sp + static_cast<uint32_t>((q + 1) * 32), sb);
+            reduce32(sa, q);
+            tmem_wait_ld_dep(sb);
+            if (q + 2 < kChunk / 32)
+              tmem_ld_32x32b_x32_nowait(sp + static_cast<uint32_t>((q + 2) * 32), sa);
+            reduce32(sb, q + 1);
           }
         }
         // running max; O is rescaled only when the max grows by more than 2^8
