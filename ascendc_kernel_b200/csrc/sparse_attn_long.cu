@@ -65,7 +65,9 @@ constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
 static_assert(kRows * kD * 2 == 2 * kMaxNkv * 4, "output staging reuses a log2-count buffer");
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleLog2 = 8.0f;  // O is rescaled when the max grows by more than 2^8
+// The softmax reference max moves (and O is rescaled) only when a group's max
+// exceeds it by more than 2^32.
+constexpr float kRescaleLog2 = 32.0f;
 
 struct Params {
   int64_t m;               // tokens per batch
@@ -384,96 +386,112 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t == 0) mbar_arrive(&cnt_empty[w]);
       // ---- chunks
       float m_run = sink2, l_run = 0.f;
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
       for (int c = 0; ok && c < nc; ++c, ++g) {
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], g & 1, abort_flag, p.err,
                                                DSA_DEVERR_SA_WAIT));
         if (!ok) break;
         tc_fence_after();
         const float* cb = my_bias + c * kChunk;
-        // pass 1: max over the chunk of z = s scale log2e + log2 c (-inf if c = 0);
-        // log2 c is a shared-memory broadcast per 4 keys. The next 32 columns load
-        // while the current 32 are reduced.
-        float mx = -INFINITY;
-        {
-          uint32_t sa[32], sb[32];
-          auto reduce32 = [&](const uint32_t (&v)[32], int q) {
-#pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-              const float4 bv = reinterpret_cast<const float4*>(cb + q * 32)[q4];
-              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 0]), p.scale_log2, bv.x));
-              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 1]), p.scale_log2, bv.y));
-              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 2]), p.scale_log2, bv.z));
-              mx = fmaxf(mx, fmaf(__uint_as_float(v[4 * q4 + 3]), p.scale_log2, bv.w));
-            }
-          };
-          tmem_ld_32x32b_x32_nowait(sp, sa);
-#pragma unroll 1
-          for (int q = 0; q < kChunk / 32; q += 2) {
-            tmem_wait_ld_dep(sa);
-            tmem_ld_32x32b_x32_nowait(sp + static_cast<uint32_t>((q + 1) * 32), sb);
-            reduce32(sa, q);
-            tmem_wait_ld_dep(sb);
-            if (q + 2 < kChunk / 32)
-              tmem_ld_32x32b_x32_nowait(sp + static_cast<uint32_t>((q + 2) * 32), sa);
-            reduce32(sb, q + 1);
-          }
-        }
-        // running max; O is rescaled only when the max grows by more than 2^8
-        float factor = 1.f;
-        if (c == 0) {
-          m_run = fmaxf(m_run, mx);
-        } else if (mx > m_run + kRescaleLog2) {
-          factor = ex2_approx(m_run - mx);
-          m_run = mx;
-          l_run *= factor;
-        }
-        if (c > 0 && __any_sync(0xFFFFFFFFu, factor != 1.f)) {
-          // O holds every earlier chunk's product: this chunk's S was issued
-          // after the previous PV product completed
-          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
-                                                 DSA_DEVERR_SA_WAIT));
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll 1
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) ov[k] = __float_as_uint(__uint_as_float(ov[k]) * factor);
-            tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
-          }
-        }
-        // pass 2: P = 2^(z - m) = c_k 2^(s' - m) as bf16 hi + lo over the S columns of
-        // the same keys: keys [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in
-        // [32h+16, 32h+32); each group of 32 columns is read before it is written
-        const float negm = -m_run;
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        // One pass over the chunk in groups of 32 keys: z = s scale log2e + log2 c
+        // (-inf if c = 0), then P = 2^(z - m) with m the running reference. m only
+        // moves up when a group's max exceeds it by more than 2^kRescaleLog2, so
+        // P <= 2^kRescaleLog2 c and keys flushed to 0 are below 2^-126 of the max.
+        // P goes over the S columns of the same keys as bf16 hi + lo: keys
+        // [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in [32h+16, 32h+32).
+        uint64_t ls2[2] = {0ull, 0ull};  // partial sums of P, two f32x2 accumulators
 #pragma unroll 1
         for (int hh = 0; hh < kChunk / 32; ++hh) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(hh * 32), sv);
-          uint32_t pk[32];
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(hh * 32), v);
+          uint64_t z[16];
 #pragma unroll
           for (int q4 = 0; q4 < 8; ++q4) {
             const float4 bv = reinterpret_cast<const float4*>(cb + hh * 32)[q4];
-            const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
-            float e[4];
+            z[2 * q4] = f2_fma(f2_pack(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1])),
+                               scale2, f2_pack(bv.x, bv.y));
+            z[2 * q4 + 1] =
+                f2_fma(f2_pack(__uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3])),
+                       scale2, f2_pack(bv.z, bv.w));
+          }
+          float gm0 = -INFINITY, gm1 = -INFINITY;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              e[u] = ex2_approx(fmaf(__uint_as_float(sv[4 * q4 + u]), p.scale_log2, bb[u]) + negm);
-              ls[u] += e[u];
-            }
+          for (int i = 0; i < 16; i += 2) {
+            float a0, a1, b0, b1;
+            f2_unpack(z[i], a0, a1);
+            f2_unpack(z[i + 1], b0, b1);
+            gm0 = fmax3(gm0, a0, a1);
+            gm1 = fmax3(gm1, b0, b1);
+          }
+          const float gm = fmaxf(gm0, gm1);
+          if (c == 0 && hh == 0) {
+            m_run = fmaxf(m_run, gm);  // nothing accumulated yet for this item
+          } else {
+            const bool up = gm > m_run + kRescaleLog2;
+            if (__any_sync(0xFFFFFFFFu, up)) {
+              // rare: rescale O (complete: this chunk's S was issued after the
+              // previous PV product completed), the sums and this chunk's P so far
+              const float factor = up ? ex2_approx(m_run - gm) : 1.f;
+              if (up) m_run = gm;
+              l_run *= factor;
+              const uint64_t f2 = f2_pack(factor, factor);
+              ls2[0] = f2_mul(ls2[0], f2);
+              ls2[1] = f2_mul(ls2[1], f2);
+              tmem_wait_st();
+              if (c > 0) {
+#pragma unroll 1
+                for (int q4 = 0; q4 < 4; ++q4) {
+                  uint32_t ov[32];
+                  tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
 #pragma unroll
-            for (int u2 = 0; u2 < 2; ++u2) {
-              const uint32_t h2 = pack_bf16x2(e[2 * u2], e[2 * u2 + 1]);
-              pk[2 * q4 + u2] = h2;
-              pk[16 + 2 * q4 + u2] = pack_bf16x2(e[2 * u2] - bf16_bits_to_float(h2 & 0xFFFFu),
-                                                 e[2 * u2 + 1] - bf16_bits_to_float(h2 >> 16));
+                  for (int k = 0; k < 32; ++k)
+                    ov[k] = __float_as_uint(__uint_as_float(ov[k]) * factor);
+                  tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
+                }
+              }
+#pragma unroll 1
+              for (int h2 = 0; h2 < hh; ++h2) {
+                uint32_t pv[32];
+                tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(h2 * 32), pv);
+#pragma unroll
+                for (int k2 = 0; k2 < 16; ++k2) {
+                  const float e0 = (bf16_bits_to_float(pv[k2] & 0xFFFFu) +
+                                    bf16_bits_to_float(pv[16 + k2] & 0xFFFFu)) * factor;
+                  const float e1 = (bf16_bits_to_float(pv[k2] >> 16) +
+                                    bf16_bits_to_float(pv[16 + k2] >> 16)) * factor;
+                  const uint32_t hb = pack_bf16x2(e0, e1);
+                  pv[k2] = hb;
+                  pv[16 + k2] = pack_bf16x2(e0 - bf16_bits_to_float(hb & 0xFFFFu),
+                                            e1 - bf16_bits_to_float(hb >> 16));
+                }
+                tmem_st_32x32b_x32(sp + static_cast<uint32_t>(h2 * 32), pv);
+              }
             }
+          }
+          const uint64_t negm2 = f2_pack(-m_run, -m_run);
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float d0, d1;
+            f2_unpack(f2_add(z[i], negm2), d0, d1);
+            const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);  // 2^-inf = 0
+            const uint64_t e2 = f2_pack(e0, e1);
+            ls2[i & 1] = f2_add(ls2[i & 1], e2);
+            const uint32_t hb = pack_bf16x2(e0, e1);
+            pk[i] = hb;
+            float r0, r1;
+            f2_unpack(f2_sub(e2, f2_pack(__uint_as_float(hb << 16), __uint_as_float(hb & 0xFFFF0000u))),
+                      r0, r1);
+            pk[16 + i] = pack_bf16x2(r0, r1);
           }
           tmem_st_32x32b_x32_nowait(sp + static_cast<uint32_t>(hh * 32), pk);
         }
-        l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(ls2[0], a0, a1);
+          f2_unpack(ls2[1], b0, b1);
+          l_run += (a0 + a1) + (b0 + b1);
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[w]);

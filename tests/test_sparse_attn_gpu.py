@@ -149,3 +149,26 @@ def test_long_kv_pool_all_masked_token(cuda_device):
     idx[0, 1] = -1  # token 1 attends to the sink only: output 0
     r, got = run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device, LONG_MAX_MISMATCH_FRAC)
     assert np.all(got.reshape(1, 4, 64, 128)[0, 1] == 0)
+
+
+@pytest.mark.parametrize("order", ["rising", "falling"])
+def test_long_kv_pool_wide_score_range(cuda_device, order):
+    """Scores spanning ~130 log2 units across the pool: with rising scores every
+    later 32-key group can exceed the running softmax reference by more than 2^32,
+    which rescales O, the partial sums and the chunk's P written so far; with
+    falling scores most keys underflow against the first group's max."""
+    g = torch.Generator().manual_seed(77)
+    b, m, h, nkv, topk = 1, 8, 64, 2048, 1024
+    u = torch.where(torch.rand(128, generator=g) < 0.5, -1.0, 1.0)
+    q = (u.expand(b, m, h, 128) * (1 + 0.05 * torch.randn(b, m, h, 128, generator=g)))
+    alpha = torch.linspace(0.0, 8.0, nkv)
+    if order == "falling":
+        alpha = alpha.flip(0)
+    kv = alpha[:, None] * u[None, :] * (1 + 0.05 * torch.randn(nkv, 128, generator=g))
+    q = q.to(torch.bfloat16)
+    kv = kv[None].to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(nkv, generator=g)[:topk] for _ in range(m)])[None]
+    idx = idx.to(torch.int32)
+    sink = torch.zeros(h, dtype=torch.float32)
+    r, _ = run_and_compare(q, kv, idx, sink, 128 ** -0.5, cuda_device, LONG_MAX_MISMATCH_FRAC)
+    assert r["max_abs"] <= 2.0 ** -4, r  # outputs reach |8|: at most one bf16 ulp there
