@@ -114,6 +114,20 @@ __device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bo
   return out != 0u;
 }
 
+// Named barrier that ORs a per-thread flag over the participants.
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, bool flag) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}\n"
+      : "=r"(out)
+      : "r"(flag ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return out != 0u;
+}
+
 // ---------------------------------------------------------------- proxies
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

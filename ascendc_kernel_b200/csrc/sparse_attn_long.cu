@@ -59,7 +59,8 @@ constexpr int kOffKV = kOffQ + 2 * kQBytes;                     // 65536
 constexpr int kOffBias = kOffKV + kKVStages * kKVBytes;         // 131072: [2 wg][2 tok][n] f32
 constexpr int kOffCnt = kOffBias + 2 * 2 * kMaxNkv * 4;         // 196608: [2 wg][2 tok][n] u16
 constexpr int kOffMeta = kOffCnt + 2 * 2 * kMaxNkv * 2;         // 229376
-constexpr int kOffBar = kOffMeta + 64;
+constexpr int kOffX = kOffMeta + 64;                            // [2 half][128 rows] f32
+constexpr int kOffBar = kOffX + 2 * kRows * 4;
 constexpr int kNumBars = 2 + 2 + 4 + 2 + 2 + 2 * kKVStages + 2 * 3 + 2 + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
@@ -100,9 +101,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_full = bars + 12;                 // [kKVStages]
   uint64_t* kv_empty = kv_full + kKVStages;      // [kKVStages]
   uint64_t* s_full = kv_empty + kKVStages;       // [2] S of a chunk in TMEM
-  uint64_t* p_full = s_full + 2;                 // [2] P written (128 arrivals)
+  uint64_t* p_full = s_full + 2;                 // [2] P written (256 arrivals)
   uint64_t* o_done = p_full + 2;                 // [2] PV product of a chunk completed
-  uint64_t* o_empty = o_done + 2;                // [2] O read by the epilogue (128 arrivals)
+  uint64_t* o_empty = o_done + 2;                // [2] O read by the epilogue (256 arrivals)
   uint64_t* drain_bar = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
@@ -123,11 +124,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&meta_full[2 * w + 1], 1);
       mbar_init(&cnt_empty[w], 1);
       mbar_init(&meta_empty[w], 2);
-      mbar_init(&o_empty[w], 128);
+      mbar_init(&o_empty[w], 256);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_done[i], 1);
     }
     for (int s = 0; s < kKVStages; ++s) {
@@ -331,40 +332,193 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain(drain_bar, 0);
     }
   } else if (warp < 10) {
-    // ------------------------------------------------------------ softmax warpgroups
-    const int w = (warp - 2) >> 2;
-    const int t = threadIdx.x - 64 - 128 * w;   // 0..127
+    // ------------------------------------------------------------ softmax warps
+    // Both warpgroups serve both tiles: a thread owns one row and one half of the
+    // keys of every chunk (warps 2..5 keys [0, 64), warps 6..9 keys [64, 128)) and
+    // the same half of the O columns in the epilogue. The two threads of a row
+    // sit in warps with the same TMEM lane quarter and pair up through a 64-thread
+    // named barrier per quarter.
+    const int half = (warp - 2) >> 2;
+    const int t = threadIdx.x - 64;             // 0..255
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;        // (token, head) row of the tile
     const int tok = row / p.heads;
     const int h = row % p.heads;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t sp = tmem + lane_off + static_cast<uint32_t>(w) * 256u;  // S / P
-    const uint32_t od = sp + static_cast<uint32_t>(kChunk);                  // O
     const float sink2 = p.sink[h] * kLog2e;
-    float* wbias = bias + w * 2 * kMaxNkv;                 // this warpgroup's [2 tok][n]
-    const float* my_bias = wbias + tok * kMaxNkv;
-    uint32_t* wcnt = cnt32 + w * kMaxNkv;                  // [2 tok][n / 2] words
-    uint8_t* stage = reinterpret_cast<uint8_t*>(wbias);    // output staging after the chunks
-    const uint32_t bar_id = 1 + w;
+    const uint32_t pair_bar = 4 + static_cast<uint32_t>(quarter);
+    float* xbuf = reinterpret_cast<float*>(smem + kOffX);  // [2 half][128 rows]
+    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
     bool ok = true;
-    int li = 0, g = 0;
+    int li = 0;
+    int g0 = 0, g1 = 0;  // chunks processed per tile (all items)
+
+    // One chunk of tile w: S of this thread's 64 keys, z = s scale log2e + log2 c
+    // (-inf if c = 0), P = 2^(z - m) as bf16 hi + lo over the S columns of the
+    // same keys (keys [32j, 32j+32) -> P_hi in columns [32j, 32j+16), P_lo in
+    // [32j+16, 32j+32)). The reference m of a row is agreed by its two threads:
+    // it is set from the item's first chunk and moves (rescaling O and the sum)
+    // only when a chunk's max exceeds it by more than 2^kRescaleLog2, so P <=
+    // 2^kRescaleLog2 c and keys flushed to 0 are below 2^-126 of the max.
+    auto chunk = [&](int w, int c, float& m, float& l, int& gw) -> bool {
+      // the row's two threads leave together (they meet at the pair barrier below)
+      if (!named_bar_and(pair_bar, 64, mbar_wait(&s_full[w], gw & 1, abort_flag, p.err,
+                                                 DSA_DEVERR_SA_WAIT)))
+        return false;
+      tc_fence_after();
+      const uint32_t sp = tmem + lane_off + static_cast<uint32_t>(w * 256 + half * 64);
+      const uint32_t od = tmem + lane_off + static_cast<uint32_t>(w * 256 + kChunk + half * 64);
+      const float* cb = bias + (w * 2 + tok) * kMaxNkv + c * kChunk + half * 64;
+      uint64_t z[32];
+      float mh;
+      {
+        uint32_t va[32], vb[32];
+        tmem_ld_32x32b_x32_nowait(sp, va);
+        tmem_ld_32x32b_x32_nowait(sp + 32u, vb);
+        tmem_wait_ld_dep(va);
+        tmem_wait_ld_dep(vb);
+#pragma unroll
+        for (int q4 = 0; q4 < 16; ++q4) {
+          const float4 bv = reinterpret_cast<const float4*>(cb)[q4];
+          const uint32_t* v = q4 < 8 ? va : vb;
+          const int o = (q4 & 7) * 4;
+          z[2 * q4] = f2_fma(f2_pack(__uint_as_float(v[o]), __uint_as_float(v[o + 1])), scale2,
+                             f2_pack(bv.x, bv.y));
+          z[2 * q4 + 1] = f2_fma(f2_pack(__uint_as_float(v[o + 2]), __uint_as_float(v[o + 3])),
+                                 scale2, f2_pack(bv.z, bv.w));
+        }
+        float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float a0, a1, b0, b1;
+          f2_unpack(z[i], a0, a1);
+          f2_unpack(z[i + 1], b0, b1);
+          m0 = fmax3(m0, a0, a1);
+          m1 = fmax3(m1, b0, b1);
+        }
+        mh = fmaxf(m0, m1);
+      }
+      // the item's first chunk always agrees a reference; later chunks only when
+      // some row of the quarter went more than 2^kRescaleLog2 above its reference
+      if (named_bar_or(pair_bar, 64, c == 0 || mh > m + kRescaleLog2)) {
+        xbuf[half * kRows + row] = mh;
+        named_bar_sync(pair_bar, 64);
+        const float mx = fmaxf(mh, xbuf[(half ^ 1) * kRows + row]);
+        float factor = 1.f;
+        if (c == 0) {
+          m = fmaxf(m, mx);  // nothing accumulated yet for this item
+        } else if (mx > m + kRescaleLog2) {
+          factor = ex2_approx(m - mx);
+          m = mx;
+          l *= factor;
+        }
+        if (__any_sync(0xFFFFFFFFu, factor != 1.f)) {
+          // O holds every earlier chunk's product: this chunk's S was issued
+          // after the previous PV product completed
+#pragma unroll 1
+          for (int q = 0; q < 2; ++q) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q * 32), ov);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) ov[k] = __float_as_uint(__uint_as_float(ov[k]) * factor);
+            tmem_st_32x32b_x32(od + static_cast<uint32_t>(q * 32), ov);
+          }
+        }
+      }
+      const uint64_t negm2 = f2_pack(-m, -m);
+      uint64_t ls2[2] = {0ull, 0ull};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float d0, d1;
+          f2_unpack(f2_add(z[16 * j + i], negm2), d0, d1);
+          const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);  // 2^-inf = 0
+          const uint64_t e2 = f2_pack(e0, e1);
+          ls2[i & 1] = f2_add(ls2[i & 1], e2);
+          const uint32_t hb = pack_bf16x2(e0, e1);
+          pk[i] = hb;
+          float r0, r1;
+          f2_unpack(f2_sub(e2, f2_pack(__uint_as_float(hb << 16), __uint_as_float(hb & 0xFFFF0000u))),
+                    r0, r1);
+          pk[16 + i] = pack_bf16x2(r0, r1);
+        }
+        tmem_st_32x32b_x32_nowait(sp + static_cast<uint32_t>(j * 32), pk);
+      }
+      float a0, a1, b0, b1;
+      f2_unpack(ls2[0], a0, a1);
+      f2_unpack(ls2[1], b0, b1);
+      l += (a0 + a1) + (b0 + b1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[w]);
+      ++gw;
+      return true;
+    };
+
+    // Epilogue of tile w: O / (l + sink term) -> bf16 -> staging box `half` (SW128).
+    auto epilogue = [&](int w, int nc, bool valid, float m, float l) {
+      // the row's total: this thread's half plus its partner's
+      xbuf[half * kRows + row] = l;
+      named_bar_sync(pair_bar, 64);
+      const float lt = l + xbuf[(half ^ 1) * kRows + row];
+      if (ok && valid) {
+        const float inv = 1.0f / (lt + ex2_approx(sink2 - m));
+        const uint32_t od = tmem + lane_off + static_cast<uint32_t>(w * 256 + kChunk + half * 64);
+        uint8_t* stage = smem + kOffBias + w * 2 * kMaxNkv * 4;
+        const uint32_t box_row = smem_u32(stage) + static_cast<uint32_t>(half * kQBoxBytes + row * 128);
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t ov[32];
+          if (nc > 0) {
+            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(cc) * 32u, ov);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) ov[k] = 0u;  // only the sink: the output is 0
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t c16 = static_cast<uint32_t>(cc * 4 + j);
+            uint32_t wv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              wv[u] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * u]) * inv,
+                                  __uint_as_float(ov[8 * j + 2 * u + 1]) * inv);
+            st_shared_v4(box_row + ((c16 ^ static_cast<uint32_t>(row & 7)) << 4), wv[0], wv[1],
+                         wv[2], wv[3]);
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      if (nc > 0) {
+        tc_fence_before();
+        mbar_arrive(&o_empty[w]);
+      }
+    };
+
     for (int64_t item = blockIdx.x; item < p.total_items; item += gridDim.x, ++li) {
-      int b, tb;
-      bool valid;
-      tile_of(item, w, b, tb, valid);
-      // the previous item's output has left the staging buffer
+      int b, tb0, tb1;
+      bool valid0, valid1;
+      tile_of(item, 0, b, tb0, valid0);
+      tile_of(item, 1, b, tb1, valid1);
+      // the previous item's outputs have left the staging buffers
       if (t == 0) bulk_wait_group_read<0>();
-      const bool okm = mbar_wait(&meta_full[2 * w + (li & 1)], (li >> 1) & 1, abort_flag, p.err,
-                                 DSA_DEVERR_SA_WAIT);
-      ok = named_bar_and(bar_id, 128, okm);
+      const bool okm =
+          mbar_wait(&meta_full[li & 1], (li >> 1) & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT) &&
+          mbar_wait(&meta_full[2 + (li & 1)], (li >> 1) & 1, abort_flag, p.err, DSA_DEVERR_SA_WAIT);
+      ok = named_bar_and(1, 256, okm);
       if (!ok) break;
-      const int nc = meta[2 * w + (li & 1)];
+      const int nc0 = meta[li & 1], nc1 = meta[2 + (li & 1)];
       // ---- counts -> log2(c) per key (-inf for c = 0), zeroing the counters;
       // the softmax weight c e^s becomes 2^(s log2e + log2 c)
-      if (nc > 0) {
+#pragma unroll 1
+      for (int w = 0; w < 2; ++w) {
+        const int nc = w ? nc1 : nc0;
         const int n8 = nc * (kChunk / 8);  // 8-key groups per token
-        for (int i = t; i < p.tpt * n8; i += 128) {
+        uint32_t* wcnt = cnt32 + w * kMaxNkv;
+        float* wbias = bias + w * 2 * kMaxNkv;
+        for (int i = t; i < p.tpt * n8; i += 256) {
           const int tk = i / n8, q8 = i - tk * n8;
           uint4* cp = reinterpret_cast<uint4*>(wcnt + tk * (kMaxNkv / 2)) + q8;
           const uint4 v = *cp;
@@ -373,172 +527,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           float f[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const uint32_t c = (wd[u >> 1] >> ((u & 1) * 16)) & 0xFFFFu;
-            f[u] = c ? 0.f : -INFINITY;
-            if (c > 1) f[u] = log2f(static_cast<float>(c));
+            const uint32_t cnt = (wd[u >> 1] >> ((u & 1) * 16)) & 0xFFFFu;
+            f[u] = cnt ? 0.f : -INFINITY;
+            if (cnt > 1) f[u] = log2f(static_cast<float>(cnt));
           }
           float4* bp = reinterpret_cast<float4*>(wbias + tk * kMaxNkv) + q8 * 2;
           bp[0] = make_float4(f[0], f[1], f[2], f[3]);
           bp[1] = make_float4(f[4], f[5], f[6], f[7]);
         }
       }
-      named_bar_sync(bar_id, 128);
-      if (t == 0) mbar_arrive(&cnt_empty[w]);
-      // ---- chunks
-      float m_run = sink2, l_run = 0.f;
-      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
-      for (int c = 0; ok && c < nc; ++c, ++g) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], g & 1, abort_flag, p.err,
+      named_bar_sync(1, 256);
+      if (t == 0) {
+        mbar_arrive(&cnt_empty[0]);
+        mbar_arrive(&cnt_empty[1]);
+      }
+      // ---- chunks, alternating tiles (the issuer's order)
+      float m0 = sink2, l0 = 0.f, m1 = sink2, l1 = 0.f;
+      const int ncm = max(nc0, nc1);
+      for (int c = 0; ok && c < ncm; ++c) {
+        if (c < nc0) ok = chunk(0, c, m0, l0, g0);
+        if (ok && c < nc1) ok = chunk(1, c, m1, l1, g1);
+      }
+      // ---- epilogues: every chunk product of both tiles complete first, so
+      // no thread still reads the exchange buffer or a log2-count buffer
+      if (ok && nc0 > 0)
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[0], (g0 - 1) & 1, abort_flag, p.err,
                                                DSA_DEVERR_SA_WAIT));
-        if (!ok) break;
-        tc_fence_after();
-        const float* cb = my_bias + c * kChunk;
-        // One pass over the chunk in groups of 32 keys: z = s scale log2e + log2 c
-        // (-inf if c = 0), then P = 2^(z - m) with m the running reference. m only
-        // moves up when a group's max exceeds it by more than 2^kRescaleLog2, so
-        // P <= 2^kRescaleLog2 c and keys flushed to 0 are below 2^-126 of the max.
-        // P goes over the S columns of the same keys as bf16 hi + lo: keys
-        // [32h, 32h+32) -> P_hi in columns [32h, 32h+16), P_lo in [32h+16, 32h+32).
-        uint64_t ls2[2] = {0ull, 0ull};  // partial sums of P, two f32x2 accumulators
-#pragma unroll 1
-        for (int hh = 0; hh < kChunk / 32; ++hh) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(hh * 32), v);
-          uint64_t z[16];
-#pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4) {
-            const float4 bv = reinterpret_cast<const float4*>(cb + hh * 32)[q4];
-            z[2 * q4] = f2_fma(f2_pack(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1])),
-                               scale2, f2_pack(bv.x, bv.y));
-            z[2 * q4 + 1] =
-                f2_fma(f2_pack(__uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3])),
-                       scale2, f2_pack(bv.z, bv.w));
-          }
-          float gm0 = -INFINITY, gm1 = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 16; i += 2) {
-            float a0, a1, b0, b1;
-            f2_unpack(z[i], a0, a1);
-            f2_unpack(z[i + 1], b0, b1);
-            gm0 = fmax3(gm0, a0, a1);
-            gm1 = fmax3(gm1, b0, b1);
-          }
-          const float gm = fmaxf(gm0, gm1);
-          if (c == 0 && hh == 0) {
-            m_run = fmaxf(m_run, gm);  // nothing accumulated yet for this item
-          } else {
-            const bool up = gm > m_run + kRescaleLog2;
-            if (__any_sync(0xFFFFFFFFu, up)) {
-              // rare: rescale O (complete: this chunk's S was issued after the
-              // previous PV product completed), the sums and this chunk's P so far
-              const float factor = up ? ex2_approx(m_run - gm) : 1.f;
-              if (up) m_run = gm;
-              l_run *= factor;
-              const uint64_t f2 = f2_pack(factor, factor);
-              ls2[0] = f2_mul(ls2[0], f2);
-              ls2[1] = f2_mul(ls2[1], f2);
-              tmem_wait_st();
-              if (c > 0) {
-#pragma unroll 1
-                for (int q4 = 0; q4 < 4; ++q4) {
-                  uint32_t ov[32];
-                  tmem_ld_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
-#pragma unroll
-                  for (int k = 0; k < 32; ++k)
-                    ov[k] = __float_as_uint(__uint_as_float(ov[k]) * factor);
-                  tmem_st_32x32b_x32(od + static_cast<uint32_t>(q4 * 32), ov);
-                }
-              }
-#pragma unroll 1
-              for (int h2 = 0; h2 < hh; ++h2) {
-                uint32_t pv[32];
-                tmem_ld_32x32b_x32(sp + static_cast<uint32_t>(h2 * 32), pv);
-#pragma unroll
-                for (int k2 = 0; k2 < 16; ++k2) {
-                  const float e0 = (bf16_bits_to_float(pv[k2] & 0xFFFFu) +
-                                    bf16_bits_to_float(pv[16 + k2] & 0xFFFFu)) * factor;
-                  const float e1 = (bf16_bits_to_float(pv[k2] >> 16) +
-                                    bf16_bits_to_float(pv[16 + k2] >> 16)) * factor;
-                  const uint32_t hb = pack_bf16x2(e0, e1);
-                  pv[k2] = hb;
-                  pv[16 + k2] = pack_bf16x2(e0 - bf16_bits_to_float(hb & 0xFFFFu),
-                                            e1 - bf16_bits_to_float(hb >> 16));
-                }
-                tmem_st_32x32b_x32(sp + static_cast<uint32_t>(h2 * 32), pv);
-              }
-            }
-          }
-          const uint64_t negm2 = f2_pack(-m_run, -m_run);
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float d0, d1;
-            f2_unpack(f2_add(z[i], negm2), d0, d1);
-            const float e0 = ex2_approx(d0), e1 = ex2_approx(d1);  // 2^-inf = 0
-            const uint64_t e2 = f2_pack(e0, e1);
-            ls2[i & 1] = f2_add(ls2[i & 1], e2);
-            const uint32_t hb = pack_bf16x2(e0, e1);
-            pk[i] = hb;
-            float r0, r1;
-            f2_unpack(f2_sub(e2, f2_pack(__uint_as_float(hb << 16), __uint_as_float(hb & 0xFFFF0000u))),
-                      r0, r1);
-            pk[16 + i] = pack_bf16x2(r0, r1);
-          }
-          tmem_st_32x32b_x32_nowait(sp + static_cast<uint32_t>(hh * 32), pk);
-        }
-        {
-          float a0, a1, b0, b1;
-          f2_unpack(ls2[0], a0, a1);
-          f2_unpack(ls2[1], b0, b1);
-          l_run += (a0 + a1) + (b0 + b1);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full[w]);
-      }
-      // ---- epilogue: O / (l + sink term) -> bf16 -> staging (SW128) -> TMA store.
-      // Every thread's log2-count reads precede its P of the last chunk, so once
-      // that chunk's product completed the buffer is free for staging.
-      if (ok && nc > 0) {
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[w], (g - 1) & 1, abort_flag, p.err,
+      if (ok && nc1 > 0)
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_done[1], (g1 - 1) & 1, abort_flag, p.err,
                                                DSA_DEVERR_SA_WAIT));
+      if (ok) tc_fence_after();
+      epilogue(0, nc0, valid0, m0, l0);
+      if (!named_bar_and(1, 256, ok)) break;
+      if (t == 0 && valid0) {
+        uint8_t* stage = smem + kOffBias;
+        tma_store_3d(&tm_out, stage, 0, tb0 * kRows, b);
+        tma_store_3d(&tm_out, stage + kQBoxBytes, 64, tb0 * kRows, b);
+        bulk_commit_group();
       }
-      if (ok && valid) {
-        const float inv = 1.0f / (l_run + ex2_approx(sink2 - m_run));
-        if (nc > 0) tc_fence_after();
-        const uint32_t ob_row = smem_u32(stage) + static_cast<uint32_t>(row) * 128u;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t ov[32];
-          if (nc > 0) {
-            tmem_ld_32x32b_x32(od + static_cast<uint32_t>(cc) * 32u, ov);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k) ov[k] = 0u;  // only the sink: the output is 0
-          }
-          const uint32_t box_addr = ob_row + static_cast<uint32_t>(cc >> 1) * kQBoxBytes;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t chunk = static_cast<uint32_t>((cc & 1) * 4 + j);
-            uint32_t wv[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              wv[u] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * u]) * inv,
-                                  __uint_as_float(ov[8 * j + 2 * u + 1]) * inv);
-            st_shared_v4(box_addr + ((chunk ^ static_cast<uint32_t>(row & 7)) << 4), wv[0], wv[1],
-                         wv[2], wv[3]);
-          }
-        }
-        if (nc > 0) {
-          tc_fence_before();
-          mbar_arrive(&o_empty[w]);
-        }
-        fence_proxy_async_smem();
-      }
-      if (!named_bar_and(bar_id, 128, ok)) break;
-      if (t == 0 && valid) {
-        tma_store_3d(&tm_out, stage, 0, tb * kRows, b);
-        tma_store_3d(&tm_out, stage + kQBoxBytes, 64, tb * kRows, b);
+      epilogue(1, nc1, valid1, m1, l1);
+      if (!named_bar_and(1, 256, ok)) break;
+      if (t == 0 && valid1) {
+        uint8_t* stage = smem + kOffBias + 2 * kMaxNkv * 4;
+        tma_store_3d(&tm_out, stage, 0, tb1 * kRows, b);
+        tma_store_3d(&tm_out, stage + kQBoxBytes, 64, tb1 * kRows, b);
         bulk_commit_group();
       }
     }
