@@ -246,3 +246,93 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
   return dsa::run_score(q, w, kv_cache, kv_batch_stride, out, scores, batch, seqlen, n_cand, topk,
                         start_pos, ratio, offset, s);
 }
+
+// ---------------------------------------------------------------- chained path
+namespace dsa {
+int launch_topk_mask(const void* scores, int64_t ld, uint32_t* mask, int words, int64_t batch,
+                     int64_t seqlen, int64_t n_cand, int topk, int64_t start_pos, int ratio,
+                     cudaStream_t stream);
+bool sa_long_supported(int heads, int head_dim, int nkv);
+int launch_sa_long_mask(const void* q, const void* kv, const uint32_t* mask, int mask_words,
+                        int64_t mask_offset, const float* sink, void* out, int64_t batch,
+                        int64_t m, int heads, int nkv, float scale, cudaStream_t stream);
+namespace {
+constexpr int64_t kMaxChainCand = 8192;
+int mask_words(int64_t n_cand) { return static_cast<int>(((n_cand + 127) / 128) * 4); }
+struct ChainLayout {
+  size_t slices, q, w, scores, mask, bytes;
+};
+ChainLayout chain_layout(int64_t batch, int64_t seqlen, int n_heads, int head_dim, int64_t n_cand) {
+  const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
+  ChainLayout l;
+  l.slices = 0;
+  l.q = l.slices + slice_region(n_heads, head_dim, static_cast<int64_t>(rows)).bytes;
+  l.w = l.q + align256(rows * n_heads * head_dim * 2);
+  l.scores = l.w + align256(rows * n_heads * 2);
+  l.mask = l.scores + align256(rows * static_cast<size_t>(n_cand) * 2);
+  l.bytes = l.mask + align256(rows * static_cast<size_t>(mask_words(n_cand)) * 4);
+  return l;
+}
+}  // namespace
+}  // namespace dsa
+
+extern "C" size_t dsa_chain_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads,
+                                            int head_dim, int64_t n_cand) {
+  if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0 || n_cand <= 0) return 0;
+  return dsa::chain_layout(batch, seqlen, n_heads, head_dim, n_cand).bytes;
+}
+
+extern "C" int dsa_chain_fwd(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                             const float* cos_tab, const float* sin_tab, const void* kv_cache,
+                             int64_t kv_batch_stride, int64_t batch, int64_t seqlen, int dim,
+                             int q_lora_rank, int ix_heads, int ix_head_dim, int rope_dim,
+                             int index_topk, int64_t start_pos, int ratio, int64_t offset,
+                             float w_scale, const void* q, const void* kv, int n_kv,
+                             int attn_heads, int attn_head_dim, const float* sink,
+                             float softmax_scale, void* out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (batch < 0 || seqlen < 0 || index_topk <= 0 || ratio <= 0 || start_pos < 0 || n_kv <= 0 ||
+      !q || !kv || !sink || !out)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seqlen == 0) return DSA_OK;
+  const int64_t rows = batch * seqlen;
+  const int64_t n_cand = (start_pos + seqlen) / ratio;
+  const int topk = static_cast<int>(index_topk < n_cand ? index_topk : n_cand);
+  if (topk <= 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (n_cand > dsa::kMaxChainCand || !dsa::sa_long_supported(attn_heads, attn_head_dim, n_kv))
+    return DSA_ERR_UNSUPPORTED;
+  if (!dsa::aligned16(q) || !dsa::aligned16(kv) || !dsa::aligned16(out)) return DSA_ERR_MISALIGNED;
+  const dsa::ChainLayout l = dsa::chain_layout(batch, seqlen, ix_heads, ix_head_dim, n_cand);
+  if (workspace == nullptr || workspace_bytes < l.bytes ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return DSA_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* qi = ws + l.q;
+  void* wi = ws + l.w;
+  void* scores = ws + l.scores;
+  uint32_t* mask = reinterpret_cast<uint32_t*>(ws + l.mask);
+  int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, qi, rows, q_lora_rank, ix_heads,
+                            ix_head_dim, rope_dim, seqlen);
+  if (st != DSA_OK) return st;
+  st = dsa::check_wproj(x, w_proj, wi, rows, dim, ix_heads);
+  if (st != DSA_OK) return st;
+  // the score checks (the buffer path writes no index list: the bitmap stands in)
+  st = dsa::check_score(qi, wi, kv_cache, kv_batch_stride, reinterpret_cast<const int64_t*>(mask),
+                        batch, seqlen, ix_heads, ix_head_dim, n_cand, topk, start_pos, ratio);
+  if (st != DSA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, qi, rows, q_lora_rank, ix_heads, ix_head_dim,
+                      rope_dim, seqlen, ws + l.slices, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_wproj(x, w_proj, wi, rows, dim, w_scale, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_score_topk(qi, wi, kv_cache, kv_batch_stride, nullptr, scores, batch, seqlen,
+                              n_cand, topk, start_pos, ratio, offset, s);
+  if (st != DSA_OK) return st;
+  const int words = dsa::mask_words(n_cand);
+  st = dsa::launch_topk_mask(scores, n_cand, mask, words, batch, seqlen, n_cand, topk, start_pos,
+                             ratio, s);
+  if (st != DSA_OK) return st;
+  return dsa::launch_sa_long_mask(q, kv, mask, words, offset, sink, out, batch, seqlen,
+                                  attn_heads, n_kv, softmax_scale, s);
+}

@@ -176,6 +176,146 @@ int launch_sort(const Params& p, const DeviceInfo& di, cudaStream_t stream) {
   return cuda_status(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ top-k set
+// For a consumer that only needs WHICH candidates are selected (attention in
+// the multiplicity form is order-independent): the same selection as the sort
+// (score descending, then index ascending), written as a bitmap, one bit per
+// candidate, by a radix select instead of a sort. Pass 1 histograms the high
+// byte of the 16-bit orderable score and finds the bin holding the k-th key,
+// pass 2 does the same with the low byte inside that bin, so T, the k-th key,
+// and the number of keys equal to T still to take are known; keys above T are
+// in, and keys equal to T are taken in ascending index order (a block scan of
+// per-thread tie counts over contiguous index ranges).
+constexpr int kMaskThreads = 256;
+
+struct MaskParams {
+  const uint16_t* scores;  // [rows, ld] bf16, valid for k < n(t)
+  int64_t ld;
+  uint32_t* mask;          // [rows, words]
+  int words;               // >= ceil(n_cand / 32)
+  int K;
+  int64_t S;
+  int64_t T;
+  int ratio;
+  int causal;
+  int64_t rows;
+};
+
+// Inclusive sum of v over the block's 256 threads (thread order); `tmp` holds 8 ints.
+__device__ __forceinline__ int block_incl_sum(int v, int* tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xFFFFFFFFu, v, o);
+    if (lane >= o) v += x;
+  }
+  if (lane == 31) tmp[warp] = v;
+  __syncthreads();
+  int pre = 0;
+#pragma unroll
+  for (int w = 0; w < kMaskThreads / 32; ++w) pre += w < warp ? tmp[w] : 0;
+  __syncthreads();
+  return v + pre;
+}
+
+// J: candidates per thread (contiguous), n_cand <= 256 J.
+template <int J>
+__global__ void __launch_bounds__(kMaskThreads)
+    topk_mask_kernel(const MaskParams p) {
+  __shared__ int hist[256];
+  __shared__ int tmp[8];
+  __shared__ int sel[2];  // the bin holding the k-th key, keys above it
+  __shared__ uint32_t bits[256 * J / 32];
+  const int tid = threadIdx.x;
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const int64_t t = row % p.S;
+    int64_t n64 = p.T;
+    if (p.causal) {
+      n64 = (t + 1) / p.ratio;
+      if (n64 > p.T) n64 = p.T;
+    }
+    const int n = static_cast<int>(n64);
+    uint32_t* out = p.mask + row * p.words;
+    if (n <= p.K) {  // every valid candidate is selected
+      for (int i = tid; i < p.words; i += kMaskThreads) {
+        const int lo = i * 32;
+        out[i] = n >= lo + 32 ? 0xFFFFFFFFu : (n > lo ? (1u << (n - lo)) - 1u : 0u);
+      }
+      continue;
+    }
+    const uint16_t* src = p.scores + row * p.ld;
+    const int e0 = tid * J;
+    uint32_t key[J];  // orderable 16-bit score, or 0x10000 for "not a candidate"
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = e0 + j;
+      key[j] = e < n ? ord16(__ldg(src + e)) : 0x10000u;
+    }
+    // pass 1: the high byte of the k-th key (bins walked from the top, thread i
+    // holds bin 255 - i)
+    hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      if (key[j] < 0x10000u) atomicAdd(&hist[key[j] >> 8], 1);
+    __syncthreads();
+    int c = hist[255 - tid];
+    int incl = block_incl_sum(c, tmp);
+    if (incl >= p.K && incl - c < p.K) {
+      sel[0] = 255 - tid;
+      sel[1] = incl - c;
+    }
+    __syncthreads();
+    const int hb = sel[0];
+    const int need1 = p.K - sel[1];
+    // pass 2: the low byte, among keys whose high byte is hb
+    hist[tid] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      if (key[j] < 0x10000u && static_cast<int>(key[j] >> 8) == hb) atomicAdd(&hist[key[j] & 0xFFu], 1);
+    __syncthreads();
+    c = hist[255 - tid];
+    incl = block_incl_sum(c, tmp);
+    if (incl >= need1 && incl - c < need1) {
+      sel[0] = 255 - tid;
+      sel[1] = incl - c;
+    }
+    __syncthreads();
+    const uint32_t thr = (static_cast<uint32_t>(hb) << 8) | static_cast<uint32_t>(sel[0]);
+    const int need = need1 - sel[1];
+    // keys above thr are taken; keys equal to thr (need of them) in index order
+    int ties = 0;
+#pragma unroll
+    for (int j = 0; j < J; ++j) ties += key[j] == thr ? 1 : 0;
+    const int tie_base = block_incl_sum(ties, tmp) - ties;
+    uint32_t b = 0;
+    int ti = tie_base;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      bool take = false;
+      if (key[j] < 0x10000u) {
+        if (key[j] > thr) {
+          take = true;
+        } else if (key[j] == thr) {
+          take = ti < need;
+          ++ti;
+        }
+      }
+      b |= (take ? 1u : 0u) << j;
+    }
+    if (J == 32) {
+      bits[tid] = b;
+    } else {  // J == 16: two threads per word
+      const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, b, 1);
+      if ((tid & 1) == 0) bits[tid >> 1] = b | (other << 16);
+    }
+    __syncthreads();
+    for (int i = tid; i < p.words; i += kMaskThreads) out[i] = i < 256 * J / 32 ? bits[i] : 0u;
+    __syncthreads();
+  }
+}
+
 }  // namespace ixt
 
 // Largest candidate count the sort path takes.
@@ -204,6 +344,40 @@ int launch_topk_sort(const void* scores, int64_t ld, int64_t* out, int64_t batch
   if (n_cand <= kThreads * 4) return launch_sort<4>(p, di, stream);
   if (n_cand <= kThreads * 8) return launch_sort<8>(p, di, stream);
   return launch_sort<16>(p, di, stream);
+}
+
+}  // namespace dsa
+
+namespace dsa {
+
+// Top-k set of each token as a bitmap [rows, words] (bit k of a row: candidate k
+// is among the token's top-k by score descending, index ascending).
+int launch_topk_mask(const void* scores, int64_t ld, uint32_t* mask, int words, int64_t batch,
+                     int64_t seqlen, int64_t n_cand, int topk, int64_t start_pos, int ratio,
+                     cudaStream_t stream) {
+  using namespace ixt;
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st != DSA_OK) return st;
+  if (n_cand > kMaskThreads * 32 || words * 32 < n_cand) return DSA_ERR_UNSUPPORTED;
+  MaskParams p;
+  p.scores = static_cast<const uint16_t*>(scores);
+  p.ld = ld;
+  p.mask = mask;
+  p.words = words;
+  p.K = topk;
+  p.S = seqlen;
+  p.T = n_cand;
+  p.ratio = ratio;
+  p.causal = start_pos == 0 ? 1 : 0;
+  p.rows = batch * seqlen;
+  int64_t grid = static_cast<int64_t>(di.num_sms) * 8;
+  if (grid > p.rows) grid = p.rows;
+  if (n_cand <= kMaskThreads * 16)
+    topk_mask_kernel<16><<<static_cast<unsigned>(grid), kMaskThreads, 0, stream>>>(p);
+  else
+    topk_mask_kernel<32><<<static_cast<unsigned>(grid), kMaskThreads, 0, stream>>>(p);
+  return cuda_status(cudaGetLastError());
 }
 
 }  // namespace dsa

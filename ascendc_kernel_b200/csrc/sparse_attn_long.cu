@@ -81,7 +81,10 @@ struct Params {
   int nkv;
   float scale_log2;
   const float* sink;
-  const void* idx;         // [batch, m, topk] int32 / int64
+  const void* idx;         // [batch, m, topk] int32 / int64 (when mask is null)
+  const uint32_t* mask;    // or: [batch, m, mask_words] selection bitmaps, bit k = row k + mask_offset
+  int mask_words;
+  int64_t mask_offset;
   unsigned int* err;
 };
 
@@ -599,8 +602,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         int maxidx = -1;
         if (valid) {
           const int64_t tok0 = static_cast<int64_t>(tb) * kRows / p.heads;
-          const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
           uint32_t* wcnt = cnt32 + w * kMaxNkv;
+          if (p.mask != nullptr) {
+            // selection bitmaps (one per token): every set bit counts once
+            const uint32_t* msrc = p.mask + (static_cast<int64_t>(b) * p.m + tok0) * p.mask_words;
+            const int n_w = p.tpt * p.mask_words;
+            for (int i = ct; i < n_w; i += 64) {
+              const int tk = i / p.mask_words;
+              const int64_t kb = static_cast<int64_t>(i - tk * p.mask_words) * 32 + p.mask_offset;
+              uint32_t bits = __ldg(msrc + i);
+              while (bits) {
+                const int jb = __ffs(static_cast<int>(bits)) - 1;
+                bits &= bits - 1u;
+                const int64_t k = kb + jb;
+                if (k >= 0 && k < p.nkv) {
+                  const int kk = static_cast<int>(k);
+                  atomicAdd(&wcnt[tk * (kMaxNkv / 2) + (kk >> 1)], 1u << ((kk & 1) * 16));
+                  maxidx = max(maxidx, kk);
+                }
+              }
+            }
+          } else {
+          const IdxT* src = idx + (static_cast<int64_t>(b) * p.m + tok0) * p.topk;
           const int n_ent = p.tpt * p.topk;
           // batches of 8 independent loads ahead of their shared-memory atomics
           for (int i0 = 0; i0 < n_ent; i0 += 8 * 64) {
@@ -620,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 maxidx = max(maxidx, kk);
               }
             }
+          }
           }
         }
         maxidx = __reduce_max_sync(0xFFFFFFFFu, maxidx);
@@ -653,9 +677,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <typename IdxT>
-int launch(const void* q, const void* kv, const void* idx, const float* sink, void* out,
-           int64_t batch, int64_t m, int heads, int nkv, int topk, float scale,
-           cudaStream_t stream) {
+int launch(const void* q, const void* kv, const void* idx, const uint32_t* mask, int mask_words,
+           int64_t mask_offset, const float* sink, void* out, int64_t batch, int64_t m, int heads,
+           int nkv, int topk, float scale, cudaStream_t stream) {
   DeviceInfo di;
   int st = current_device_info(&di);
   if (st != DSA_OK) return st;
@@ -704,6 +728,9 @@ int launch(const void* q, const void* kv, const void* idx, const float* sink, vo
   p.scale_log2 = scale * kLog2e;
   p.sink = sink;
   p.idx = idx;
+  p.mask = mask;
+  p.mask_words = mask_words;
+  p.mask_offset = mask_offset;
   p.err = err;
   static bool attr_done[64] = {false};
   if (!attr_done[di.device]) {
@@ -733,8 +760,20 @@ int launch_sa_long(const void* q, const void* kv, const void* idx, int idx_elem_
                    const float* sink, void* out, int64_t batch, int64_t m, int heads, int nkv,
                    int topk, float scale, cudaStream_t stream) {
   if (idx_elem_bytes == 8)
-    return sal::launch<int64_t>(q, kv, idx, sink, out, batch, m, heads, nkv, topk, scale, stream);
-  return sal::launch<int32_t>(q, kv, idx, sink, out, batch, m, heads, nkv, topk, scale, stream);
+    return sal::launch<int64_t>(q, kv, idx, nullptr, 0, 0, sink, out, batch, m, heads, nkv, topk,
+                                scale, stream);
+  return sal::launch<int32_t>(q, kv, idx, nullptr, 0, 0, sink, out, batch, m, heads, nkv, topk,
+                              scale, stream);
+}
+
+// Long-pool SparseAttention whose per-token selection comes as bitmaps
+// [batch, m, mask_words] (bit k: pool row k + mask_offset is selected once), as
+// written by the indexer's top-k set kernel: the chained path's hand-off.
+int launch_sa_long_mask(const void* q, const void* kv, const uint32_t* mask, int mask_words,
+                        int64_t mask_offset, const float* sink, void* out, int64_t batch,
+                        int64_t m, int heads, int nkv, float scale, cudaStream_t stream) {
+  return sal::launch<int32_t>(q, kv, nullptr, mask, mask_words, mask_offset, sink, out, batch, m,
+                              heads, nkv, 0, scale, stream);
 }
 
 }  // namespace dsa

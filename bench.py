@@ -294,16 +294,22 @@ def bench_chain(dev):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) * 1e3 / n
 
+    from ascendc_kernel_b200 import chain
+
+    sam = sa.ModelNew(64, 128).to(dev)
     idx = model(x, qr, 0, 0)
     ix_us = timed(lambda: model(x, qr, 0, 0))
     sa_us = timed(lambda: sa.sparse_attn(q, pool, sink, idx, scale, out=out))
     chain_us = timed(lambda: sa.sparse_attn(q, pool, sink, model(x, qr, 0, 0), scale, out=out))
+    fused_us = timed(lambda: chain.indexer_sparse_attn(model, sam, x, qr, 0, 0, q, pool, out=out))
     valid = int((idx >= 0).sum())
     peak, peak_kind = load_peaks("bf16_tflops")
     flops = valid * 64 * 128 * 4
     sa_tflops = flops / (sa_us * 1e-6) / 1e12
     return {"indexer_us": ix_us, "sparse_attn_us": sa_us, "chain_us": chain_us,
+            "fused_chain_us": fused_us,
             "tokens_per_s": b * s_len / (chain_us * 1e-6),
+            "fused_tokens_per_s": b * s_len / (fused_us * 1e-6),
             "valid_index_pairs": valid,
             "sparse_attn_tflops": sa_tflops, "sparse_attn_frac_of_bf16_peak": sa_tflops / peak,
             "bf16_peak_source": peak_kind,

@@ -81,8 +81,11 @@ int dsa_sinkhorn_fwd(const float* x, float* y, int64_t n_mat, int n, int repeat,
  *   out    [batch, m, n_heads, head_dim] bf16
  * out[b,t,h,:] = sum_j w_j kv[b, idx_j], w = softmax over the valid j of
  * (q.kv*scale) with the sink logit in the max and the denominator.
- * Supported: head_dim == 128, n_heads in {16,32,64,128}, 1 <= n_kv <= 32,
- * topk*idx_elem_bytes a multiple of 16 and topk <= 256; q, kv, idx, out 16-byte aligned.
+ * Supported: head_dim == 128; n_heads in {16,32,64,128}, 1 <= n_kv <= 32,
+ * topk*idx_elem_bytes a multiple of 16 and topk <= 128 (one fused pass over the
+ * whole pool); or, for larger pools or lists (the chained long-context case),
+ * n_heads in {64,128}, n_kv <= 4096 and any topk (128-row pool chunks);
+ * q, kv, idx, out 16-byte aligned.
  * Replaces launch_sa_fused (src/sparse_attn_kernel_mm.asc:310-313) and its
  * pybind wrapper run_fused (src/task1_sparse_attn.py:420-429); semantics follow
  * sparse_attn_ref in reference/task1_v0_ref.py:5-24.
@@ -190,6 +193,34 @@ int dsa_indexer_fwd_noalloc(const void* x, const void* qr, const void* wq_b, con
                             int dim, int q_lora_rank, int n_heads, int head_dim, int rope_dim,
                             int index_topk, int64_t start_pos, int ratio, int64_t offset,
                             float w_scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Chained path: the indexer's top-k selection feeding SparseAttention over a kv
+ * pool in one call (x[4,16384,1024], kv_cache[4,4096,64],
+ * top-2048, then q[4,16384,64,128] over a kv pool [4,4096,128]). The result is
+ * the one of dsa_indexer_fwd followed by dsa_sparse_attn_fwd on its int64
+ * output, i.e. sparse_attn_ref(q, kv, sink, Model.forward(x, qr, start_pos,
+ * offset), scale) (reference/task2_v0_ref.py:123-144, reference/task1_v0_ref.py
+ * :5-24): attention in the multiplicity form depends only on which pool rows a
+ * token selected, so the selection travels as one bitmap per token (n_cand bits,
+ * bit k = pool row k + offset) instead of an int64 list, and no sort runs.
+ * Indexer arguments as dsa_indexer_fwd; attention arguments as
+ * dsa_sparse_attn_fwd (q [batch, seqlen, attn_heads, attn_head_dim], kv
+ * [batch, n_kv, attn_head_dim], out like q). Supported: n_cand <= 8192,
+ * attn_heads in {64,128}, attn_head_dim 128, n_kv <= 4096. workspace:
+ * dsa_chain_workspace_bytes(batch, seqlen, ix_heads, ix_head_dim, n_cand)
+ * bytes, 256-byte aligned. The reference runs the two modules one after the
+ * other; it has no fused counterpart. */
+size_t dsa_chain_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim,
+                                 int64_t n_cand);
+int dsa_chain_fwd(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                  const float* cos_tab, const float* sin_tab, const void* kv_cache,
+                  int64_t kv_batch_stride, int64_t batch, int64_t seqlen, int dim,
+                  int q_lora_rank, int ix_heads, int ix_head_dim, int rope_dim, int index_topk,
+                  int64_t start_pos, int ratio, int64_t offset, float w_scale, const void* q,
+                  const void* kv, int n_kv, int attn_heads, int attn_head_dim,
+                  const float* sink, float softmax_scale, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
