@@ -373,13 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 2);
+      mbar_init(&q_empty[i], 256);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 256);
     }
     for (int i = 0; i < kKVStages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 2);
+      mbar_init(&kv_empty[i], 256);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -623,10 +623,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
         }
-        ok = named_bar_and(1 + wg, 128, ok);
-        if (ok && t_in == 0) mbar_arrive(&kv_empty[s]);
+        // every epilogue thread releases the stage itself, so a warp busy with
+        // exact recomputations holds up no other warp
+        if (ok) mbar_arrive(&kv_empty[s]);
       }
-      if (ok && t_in == 0) mbar_arrive(&q_empty[qb]);
+      // the warpgroup leaves the unit together: its per-token arrays are rewritten next
+      ok = named_bar_and(1 + wg, 128, ok);
+      if (ok) mbar_arrive(&q_empty[qb]);
       if (gs) {  // scores go to global memory; the top-k runs in its own kernel
         if (!ok) break;
         continue;
