@@ -165,10 +165,10 @@ __device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qro
   return round_f64_to_bf16(acc);
 }
 
-// Per-warp queue of (token, kv row) pairs of the current chunk whose score
-// could not be certified. Entry: word 0 = token slot << 16 | kv row of the
-// chunk, words 1..16 = per head the bf16 pair {RNE(v+E), RNE(v-E)} of
-// the interval that holds the head's exact bf16 score.
+// Per-warp queue of (token, candidate) pairs of the last one or two chunks
+// whose score could not be certified. Entry: word 0 = kv stage << 28 | token
+// slot << 16 | candidate k, words 1..16 = per head the bf16 pair {RNE(v+E),
+// RNE(v-E)} of the interval that holds the head's exact bf16 score.
 constexpr int kRqWords = 17;
 
 __device__ __forceinline__ bool bf16_positive(uint32_t h16) {
@@ -184,14 +184,15 @@ __device__ __forceinline__ uint32_t ord_to_bf16(uint32_t ord) {
 // open and can be positive, then the exact score chain; writes the key (or,
 // with gs, the bf16 score to gs[token slot * gld + k]).
 __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
-                                         const uint8_t* kvs, int chunk_base, const float* wv,
+                                         const uint8_t* kv_stages, const float* wv,
                                          uint32_t* keys, uint16_t* gs, int64_t gld, int lane) {
   __syncwarp();
   for (int i = lane; i < n; i += 32) {
     uint32_t* e = rq + i * kRqWords;
-    const int tt = static_cast<int>(e[0] >> 16);
-    const int row = static_cast<int>(e[0] & 0xFFFFu);
-    const int k = chunk_base + row;
+    const int tt = static_cast<int>((e[0] >> 16) & 0xFFFu);
+    const int k = static_cast<int>(e[0] & 0xFFFFu);
+    const int row = k & (kChunk - 1);
+    const uint8_t* kvs = kv_stages + (e[0] >> 28) * kKVBytes;
     uint32_t open = 0;  // heads whose interval is open and can be positive
 #pragma unroll
     for (int h = 0; h < 16; ++h) {
@@ -529,6 +530,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the queue of pairs that need an exact recomputation
       uint32_t* rq = hist;
       constexpr int kRqCap = kSelBytes / 4 / kRqWords;
+      const uint8_t* kv_stages = smem + kOffKV;
+      // queued pairs are drained every second chunk (or when the queue would
+      // overflow, or at the unit's end); a thread releases a kv stage only after
+      // the pairs that read it are drained
+      int rq_n = 0;
+      int held = -1;  // stage of the previous chunk, not yet released
       for (int c = 0; ok && c < nch; ++c, ++gc) {
         const int s = gc % kKVStages;
         const int ab = gc & 1;
@@ -542,7 +549,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
           tc_fence_after();
           const float kvn = row_norm64(kvs, row) * kGamma;
-          int rq_n = 0;
           const uint32_t* wpk = reinterpret_cast<const uint32_t*>(smem + kOffWP);
           const uint32_t* psel = reinterpret_cast<const uint32_t*>(smem + kOffPS);
 #pragma unroll 1
@@ -597,12 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {
-                  drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, gs, p.score_ld, lane);
+                  drain_queue(rq, rq_n, qs, kv_stages, wv, keys, gs, p.score_ld, lane);
                   rq_n = 0;
                 }
                 if (need) {
                   uint32_t* e = rq + (rq_n + __popc(bal & ((1u << lane) - 1u))) * kRqWords;
-                  e[0] = (static_cast<uint32_t>(tt) << 16) | static_cast<uint32_t>(row);
+                  e[0] = (static_cast<uint32_t>(s) << 28) | (static_cast<uint32_t>(tt) << 16) |
+                         static_cast<uint32_t>(k);
 #pragma unroll
                   for (int h = 0; h < 16; ++h) e[1 + h] = prs[h];
                 }
@@ -618,14 +625,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (__any_sync(0xFFFFFFFFu, rq_n > 0))
-            drain_queue(rq, rq_n, qs, kvs, c * kChunk, wv, keys, gs, p.score_ld, lane);
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
+          if ((c & 1) || c == nch - 1) {
+            if (rq_n > 0) drain_queue(rq, rq_n, qs, kv_stages, wv, keys, gs, p.score_ld, lane);
+            rq_n = 0;
+          }
         }
-        // every epilogue thread releases the stage itself, so a warp busy with
+        // every epilogue thread releases its stages itself, so a warp busy with
         // exact recomputations holds up no other warp
-        if (ok) mbar_arrive(&kv_empty[s]);
+        if (ok) {
+          if (rq_n == 0) {
+            if (held >= 0) mbar_arrive(&kv_empty[held]);
+            mbar_arrive(&kv_empty[s]);
+            held = -1;
+          } else {
+            held = s;  // pairs of this chunk wait for the next drain
+          }
+        }
       }
       // the warpgroup leaves the unit together: its per-token arrays are rewritten next
       ok = named_bar_and(1 + wg, 128, ok);
