@@ -32,8 +32,9 @@ SIGNATURES = {
     "dsa_indexer_qproj_rope": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
                                       _i32, _i32, _i32, _i32, _i64, _c_void_p, _size_t,
                                       _c_void_p]),
+    "dsa_indexer_wproj_workspace_bytes": (_size_t, [_i64, _i32]),
     "dsa_indexer_wproj": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _f32,
-                                 _c_void_p]),
+                                 _c_void_p, _size_t, _c_void_p]),
     "dsa_indexer_score_topk": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i64,
                                       _i64, _i32, _i32, _i64, _i32, _i64, _i32, _i64,
                                       _c_void_p, _size_t, _c_void_p]),

@@ -12,8 +12,9 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
                       const int* b_span, uint32_t* open_bits, cudaStream_t stream);
 int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* sig, float* err,
                      float* n3, int* span, cudaStream_t stream);
-int launch_wproj(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
-                 cudaStream_t stream);
+int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
+                    void* scratch, cudaStream_t stream);
+size_t wproj_s8_scratch_bytes(int64_t rows, int K);
 int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_bstride,
                       int64_t* out, void* scores, int64_t batch, int64_t seqlen, int64_t n_cand,
                       int topk, int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream);
@@ -57,6 +58,15 @@ SliceRegion slice_region(int n_heads, int head_dim, int64_t rows) {
   r.open = r.a_span + align256(R * 4);
   r.bytes = r.open + align256(R * (N / 8));
   return r;
+}
+
+// Front of every indexer workspace: the q projection's slices (above), reused
+// afterwards (same stream) by the w projection's slices of x [rows, dim <= 1024].
+constexpr int kMaxDim = 1024;
+size_t front_bytes(int n_heads, int head_dim, int64_t rows) {
+  const size_t a = slice_region(n_heads, head_dim, rows).bytes;
+  const size_t b = wproj_s8_scratch_bytes(rows, kMaxDim);
+  return a > b ? a : b;
 }
 
 // Slices wq_b and qr into the workspace, then runs the q projection.
@@ -150,11 +160,21 @@ extern "C" int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const fl
                         static_cast<cudaStream_t>(stream));
 }
 
+extern "C" size_t dsa_indexer_wproj_workspace_bytes(int64_t rows, int dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  return dsa::wproj_s8_scratch_bytes(rows, dim);
+}
+
 extern "C" int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows,
-                                 int dim, int n_heads, float scale, void* stream) {
+                                 int dim, int n_heads, float scale, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
   int st = dsa::check_wproj(x, w_proj, w_out, rows, dim, n_heads);
   if (st != DSA_OK || rows == 0) return st;
-  return dsa::launch_wproj(x, w_proj, w_out, rows, dim, scale, static_cast<cudaStream_t>(stream));
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
+      workspace_bytes < dsa::wproj_s8_scratch_bytes(rows, dim))
+    return DSA_ERR_WORKSPACE;
+  return dsa::launch_wproj_s8(x, w_proj, w_out, rows, dim, scale, workspace,
+                              static_cast<cudaStream_t>(stream));
 }
 
 namespace dsa {
@@ -200,7 +220,7 @@ extern "C" size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int
                                               int head_dim, int64_t n_cand, int topk) {
   if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
-  return dsa::slice_region(n_heads, head_dim, static_cast<int64_t>(rows)).bytes +
+  return dsa::front_bytes(n_heads, head_dim, static_cast<int64_t>(rows)) +
          dsa::align256(rows * n_heads * head_dim * 2) + dsa::align256(rows * n_heads * 2) +
          dsa::score_buffer_bytes(batch, seqlen, n_cand, topk);
 }
@@ -225,7 +245,7 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return DSA_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  const size_t wreg = dsa::slice_region(n_heads, head_dim, rows).bytes;
+  const size_t wreg = dsa::front_bytes(n_heads, head_dim, rows);
   void* q = ws + wreg;
   void* w = ws + wreg + dsa::align256(static_cast<size_t>(rows) * n_heads * head_dim * 2);
   void* scores = static_cast<uint8_t*>(w) + dsa::align256(static_cast<size_t>(rows) * n_heads * 2);
@@ -241,7 +261,7 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
   st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
                       rope_dim, seqlen, ws, s);
   if (st != DSA_OK) return st;
-  st = dsa::launch_wproj(x, w_proj, w, rows, dim, w_scale, s);
+  st = dsa::launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, ws, s);
   if (st != DSA_OK) return st;
   return dsa::run_score(q, w, kv_cache, kv_batch_stride, out, scores, batch, seqlen, n_cand, topk,
                         start_pos, ratio, offset, s);
@@ -266,7 +286,7 @@ ChainLayout chain_layout(int64_t batch, int64_t seqlen, int n_heads, int head_di
   const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
   ChainLayout l;
   l.slices = 0;
-  l.q = l.slices + slice_region(n_heads, head_dim, static_cast<int64_t>(rows)).bytes;
+  l.q = l.slices + front_bytes(n_heads, head_dim, static_cast<int64_t>(rows));
   l.w = l.q + align256(rows * n_heads * head_dim * 2);
   l.scores = l.w + align256(rows * n_heads * 2);
   l.mask = l.scores + align256(rows * static_cast<size_t>(n_cand) * 2);
@@ -324,7 +344,7 @@ extern "C" int dsa_chain_fwd(const void* x, const void* qr, const void* wq_b, co
   st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, qi, rows, q_lora_rank, ix_heads, ix_head_dim,
                       rope_dim, seqlen, ws + l.slices, s);
   if (st != DSA_OK) return st;
-  st = dsa::launch_wproj(x, w_proj, wi, rows, dim, w_scale, s);
+  st = dsa::launch_wproj_s8(x, w_proj, wi, rows, dim, w_scale, ws + l.slices, s);
   if (st != DSA_OK) return st;
   st = dsa::launch_score_topk(qi, wi, kv_cache, kv_batch_stride, nullptr, scores, batch, seqlen,
                               n_cand, topk, start_pos, ratio, offset, s);

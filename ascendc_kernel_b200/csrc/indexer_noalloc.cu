@@ -22,7 +22,7 @@
 namespace dsa {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t{64} << 20;  // 64 MiB
+constexpr size_t kNoAllocScratchBytes = size_t{128} << 20;  // 128 MiB
 
 static __device__ __align__(256) unsigned char g_indexer_scratch[kNoAllocScratchBytes];
 

@@ -223,10 +223,12 @@ def wproj(x: torch.Tensor, wp: torch.Tensor, scale: float) -> torch.Tensor:
     x = x.contiguous()
     rows = x.numel() // x.shape[-1]
     out = torch.empty(rows, wp.shape[0], dtype=torch.bfloat16, device=x.device)
+    nbytes = lib().dsa_indexer_wproj_workspace_bytes(rows, x.shape[-1])
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
         call("dsa_indexer_wproj", x.data_ptr(), wp.contiguous().data_ptr(), out.data_ptr(), rows,
-             x.shape[-1], wp.shape[0], float(scale), stream)
+             x.shape[-1], wp.shape[0], float(scale), ws.data_ptr(), ws.numel(), stream)
     return out
 
 

@@ -120,11 +120,16 @@ int dsa_indexer_qproj_rope(const void* qr, const void* wq_b, const float* cos_ta
 
 /* (b) w = bf16(bf16(x . w_proj^T) * scale).  x [rows, dim] bf16,
  *     w_proj [n_heads, dim] bf16, w_out [rows, n_heads] bf16.
- *     Supported: n_heads == 16, dim a multiple of 64 and <= 1024.
+ *     Supported: n_heads == 16, dim a multiple of 64 and <= 1024. The dot
+ *     products are exact (int8 slices of both operands on the tensor cores);
+ *     workspace: dsa_indexer_wproj_workspace_bytes(rows, dim) bytes, 256-byte
+ *     aligned (the slices and per-row exponents).
  *     Replaces the weights_proj executor (src/task2_indexer.py:817-839);
  *     semantics reference/task2_v0_ref.py:132. */
+size_t dsa_indexer_wproj_workspace_bytes(int64_t rows, int dim);
 int dsa_indexer_wproj(const void* x, const void* w_proj, void* w_out, int64_t rows, int dim,
-                      int n_heads, float scale, void* stream);
+                      int n_heads, float scale, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 /* (c) Scores and top-k:
  *     score[t,k] = bf16( sum_h bf16( relu(bf16(q[t,h].kv[k])) * w[t,h] ) )
@@ -178,10 +183,10 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
  * allocating inside an operator, or latency-critical paths where a
  * cudaMalloc/cudaFree (which can synchronize the device) is not acceptable.
  * Same arguments and result as dsa_indexer_fwd, without the workspace: the
- * operand slices and the q and w intermediates live in a fixed 64 MiB array inside the library, one per
+ * operand slices and the q and w intermediates live in a fixed 128 MiB array inside the library, one per
  * device that loads it, held until the process exits. The request needs
  * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
- * <= 64 MiB, i.e. at most 23,219 tokens (batch*seqlen) at 16 heads x 64 dims
+ * <= 128 MiB, i.e. at most 25,961 tokens (batch*seqlen) at 16 heads x 64 dims
  * with n_cand <= 1024 and topk <= 256 (fewer with a score buffer); larger
  * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
  * device looks up the array's address; make it before any stream capture.

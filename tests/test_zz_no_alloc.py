@@ -3,7 +3,7 @@
 It serves callers that cannot allocate device memory when they call the
 indexer -- e.g. a plug-in whose host framework owns all device memory, or a
 latency-critical path that must not pay for cudaMalloc/cudaFree -- by keeping
-the q and w intermediates in a fixed 64 MiB array inside the library. These
+the q and w intermediates in a fixed 128 MiB array inside the library. These
 tests call it through the C ABI and check that two calls in a row (different
 inputs, same shared array) return exactly the indices of the workspace-taking
 entry point, dsa_indexer_fwd, and that an oversized request is rejected.
@@ -22,7 +22,7 @@ from ascendc_kernel_b200 import indexer as ix
 pytestmark = pytest.mark.gpu
 
 DSA_ERR_WORKSPACE = 5
-LIMIT_BYTES = 64 << 20  # the fixed in-library array
+LIMIT_BYTES = 128 << 20  # the fixed in-library array
 
 
 def _max_tokens():
