@@ -1,12 +1,12 @@
-// Lightning Indexer projections for sm_100a, with correctly rounded bf16 outputs.
+// Lightning Indexer q projection for sm_100a, with correctly rounded bf16 outputs.
 //
 //   q = RoPE(bf16(qr . wq_b^T))          reference/task2_v0_ref.py:129-131
-//   w = bf16(bf16(x . w_proj^T) * scale) reference/task2_v0_ref.py:132
 //
-// Both are tcgen05 GEMMs (TMA -> SW128 smem -> UMMA -> TMEM) whose epilogue
-// certifies the bf16 rounding of the exact dot product against an error bound
-// (numerics.cuh) and recomputes the few uncertain elements exactly (fp64,
-// ascending k, one lane per element) before applying RoPE / the scale.
+// (the w projection, w = bf16(bf16(x . w_proj^T) * scale), is in
+// indexer_wproj.cu). A tcgen05 GEMM (TMA -> SW128 smem -> UMMA -> TMEM) whose
+// epilogue certifies the bf16 rounding of the exact dot product against an
+// error bound and leaves the few uncertain elements to an exact fix-up before
+// applying RoPE.
 //
 // q projection kernel (one CTA per SM, persistent): exact int8 slice products
 //   (see below). Work unit = (128-row M tile, 4 heads); the A slices
@@ -16,13 +16,6 @@
 //   of 64 columns, one per epilogue warpgroup (alternate heads).
 //   warp 0 TMA, warp 1 MMA, warps 2..9 epilogue (two warpgroups, one thread
 //   per row).
-// The w projection keeps bf16 operands: its K sum is split over TMEM
-// accumulators of kKC = 32 (two K=16 MMA steps each) so that the accumulation
-// error bound stays small, and the epilogue merges the chunks in fp32.
-// w projection kernel: work unit = 128-row M tile; x streams through a
-//   4-stage ring of 128 x 64 boxes, w_proj (16 x K, K <= 1024) is resident;
-//   TMEM holds K/32 accumulators of 16 columns. The epilogue threads also read
-//   every x stage to form their row norm before the stage is released.
 #include "common.cuh"
 #include "host_util.h"
 #include "numerics.cuh"
@@ -31,16 +24,8 @@ namespace dsa {
 namespace ixp {
 
 constexpr int kBM = 128;
-constexpr int kKC = 32;
 constexpr int kBox = kBM * 128;  // 128 rows x 64 bf16 = 16 KB
 constexpr uint32_t kTmemCols = 512;
-
-// Accumulation error bound factor of the w projection (units of ||a||*||b||):
-// 3 fp32 ulps per K=16 step of a chunk (the measured worst case is ~1) plus the
-// sequential fp32 merge of the chunk sums.
-__host__ __device__ constexpr float gamma_for(int nchunks) {
-  return (3.0f * (kKC / 16) * 2.0f + static_cast<float>(nchunks)) * kTwoM24 * 1.0001f;
-}
 
 // ------------------------------------------------------------------ q proj
 // Exact slicing on the int8 tensor cores (Ozaki scheme). qr rows and wq_b rows
@@ -655,297 +640,6 @@ __global__ void __launch_bounds__(kFixWarps * 32)
   }
 }
 
-// ------------------------------------------------------------------ w proj
-constexpr int kWBN = 16;
-constexpr int kWMaxK = 1024;
-constexpr int kWStages = 4;
-constexpr int kWThreads = 192;
-constexpr int kWBBox = kWBN * 128;  // 2 KB: 16 rows x 64 bf16
-constexpr int kWOffA = 0;
-constexpr int kWOffB = kWOffA + kWStages * kBox;               // 65536
-constexpr int kWOffNB = kWOffB + (kWMaxK / 64) * kWBBox;       // 98304
-constexpr int kWQueueCap = 512;                                // per warp
-constexpr int kWOffQueue = kWOffNB + kWBN * 4;
-constexpr int kWOffBar = kWOffQueue + 4 * kWQueueCap * 4;
-constexpr int kWNumBars = 2 * kWStages + 3;
-constexpr int kWOffMisc = kWOffBar + kWNumBars * 8;
-constexpr int kWSmem = kWOffMisc + 16 + 1024;
-
-struct WParams {
-  int M;
-  int K;  // dim, multiple of 64, <= 1024
-  int m_tiles;
-  float gamma;
-  float scale;
-  const uint16_t* x;  // for the exact recomputation
-  uint16_t* w_out;
-  unsigned int* err;
-};
-
-__global__ void __launch_bounds__(kWThreads, 1)
-    wproj_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                 const WParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWOffBar);
-  uint64_t* full = bars;                  // [stages]
-  uint64_t* empty = bars + kWStages;      // [stages]: MMA commit + 128 epilogue threads
-  uint64_t* b_full = bars + 2 * kWStages;
-  uint64_t* acc_full = b_full + 1;
-  uint64_t* acc_empty = b_full + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kWOffMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kWOffMisc + 4);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int KB = p.K / 64;
-  const int nch = p.K / kKC;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + 128);
-    }
-    mbar_init(b_full, 1);
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_a);
-    tma_prefetch_desc(&tm_b);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_holder, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_holder;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(b_full, KB * kWBBox);
-      for (int kb = 0; kb < KB; ++kb)
-        tma_load_2d(smem + kWOffB + kb * kWBBox, &tm_b, kb * 64, 0, b_full);
-      int it = 0;
-      bool ok = true;
-      for (int mt = blockIdx.x; ok && mt < p.m_tiles; mt += gridDim.x) {
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % kWStages;
-          if (!mbar_wait(&empty[s], ((it / kWStages) & 1) ^ 1, abort_flag, p.err,
-                         DSA_DEVERR_GEMM_WAIT)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[s], kBox);
-          tma_load_2d(smem + kWOffA + s * kBox, &tm_a, kb * 64, mt * kBM, &full[s]);
-        }
-      }
-      mbar_drain(b_full, 0);
-      for (int i = (it > kWStages ? it - kWStages : 0); i < it; ++i)
-        mbar_drain(&full[i % kWStages], (i / kWStages) & 1);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(128, kWBN, 0, 0);
-      const uint32_t a_base = smem_u32(smem + kWOffA);
-      const uint32_t b_base = smem_u32(smem + kWOffB);
-      int it = 0, lt = 0;
-      bool ok = mbar_wait(b_full, 0, abort_flag, p.err, DSA_DEVERR_GEMM_WAIT);
-      for (int mt = blockIdx.x; ok && mt < p.m_tiles; mt += gridDim.x, ++lt) {
-        if (!mbar_wait(acc_empty, (lt & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_GEMM_WAIT)) break;
-        tc_fence_after();
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % kWStages;
-          if (!mbar_wait(&full[s], (it / kWStages) & 1, abort_flag, p.err,
-                         DSA_DEVERR_GEMM_WAIT)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const uint64_t ad = make_smem_desc(a_base + s * kBox + k4 * 32, 16u, 1024u, kLayoutSW128);
-            const uint64_t bd =
-                make_smem_desc(b_base + kb * kWBBox + k4 * 32, 16u, 1024u, kLayoutSW128);
-            const int ks = kb * 4 + k4;
-            const uint32_t chunk = static_cast<uint32_t>(ks / (kKC / 16));
-            umma_bf16(tmem + chunk * kWBN, ad, bd, idesc, (ks % (kKC / 16)) != 0 ? 1u : 0u);
-          }
-          umma_commit(&empty[s]);
-        }
-        if (!ok) break;
-        umma_commit(acc_full);
-      }
-      if (lt > 0) mbar_drain(acc_full, (lt - 1) & 1);
-    }
-  } else {
-    const int ew = warp - 2;
-    const int t = threadIdx.x - 64;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    uint32_t* queue = reinterpret_cast<uint32_t*>(smem + kWOffQueue) + ew * kWQueueCap;
-    float* nb = reinterpret_cast<float*>(smem + kWOffNB);
-    const uint8_t* b_smem = smem + kWOffB;
-    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(b_full, 0, abort_flag, p.err,
-                                                DSA_DEVERR_GEMM_WAIT));
-    if (ok && t < kWBN) {
-      float ss = 0.f;
-      for (int kb = 0; kb < KB; ++kb) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 v =
-              *reinterpret_cast<const uint4*>(b_smem + kb * kWBBox + sw128_off(t, ch));
-          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = bf16lo_to_f32(w4[e]), hi = bf16hi_to_f32(w4[e]);
-            ss = fmaf(lo, lo, ss);
-            ss = fmaf(hi, hi, ss);
-          }
-        }
-      }
-      nb[t] = norm_upper(ss, p.K);
-    }
-    ok = named_bar_and(1, 128, ok);
-    int it = 0, lt = 0;
-    for (int mt = blockIdx.x; ok && mt < p.m_tiles; mt += gridDim.x, ++lt) {
-      const int m0 = mt * kBM;
-      const bool row_valid = (m0 + row) < p.M;
-      // Row norm of x from every stage before it is released.
-      float ss = 0.f;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % kWStages;
-        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&full[s], (it / kWStages) & 1, abort_flag, p.err,
-                                               DSA_DEVERR_GEMM_WAIT));
-        if (!ok) break;
-        const uint8_t* a = smem + kWOffA + s * kBox;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 v = *reinterpret_cast<const uint4*>(a + sw128_off(row, ch));
-          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float lo = bf16lo_to_f32(w4[e]), hi = bf16hi_to_f32(w4[e]);
-            ss = fmaf(lo, lo, ss);
-            ss = fmaf(hi, hi, ss);
-          }
-        }
-        mbar_arrive(&empty[s]);
-      }
-      if (!named_bar_and(1, 128, ok)) break;
-      const float na = norm_upper(ss, p.K);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full, lt & 1, abort_flag, p.err,
-                                             DSA_DEVERR_GEMM_WAIT));
-      uint32_t flagged = 0;
-      uint32_t bits[kWBN];
-      if (ok) {
-        tc_fence_after();
-        float acc[kWBN];
-        {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(tmem + lane_off, r);
-#pragma unroll
-          for (int i = 0; i < kWBN; ++i) acc[i] = __uint_as_float(r[i]);
-        }
-        for (int c = 1; c < nch; ++c) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(tmem + lane_off + static_cast<uint32_t>(c * kWBN), r);
-#pragma unroll
-          for (int i = 0; i < kWBN; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(r[i]));
-        }
-        tc_fence_before();
-        mbar_arrive(acc_empty);
-        const float ea = p.gamma * na;
-#pragma unroll
-        for (int i = 0; i < kWBN; ++i) {
-          bits[i] = 0;
-          if (!certified_bf16(acc[i], ea * nb[i], &bits[i]) && row_valid) flagged |= 1u << i;
-        }
-        // Exact recomputation of uncertain elements, one lane per element;
-        // the x row is re-read from global memory (L2).
-        const int cnt = __popc(flagged);
-        int incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if (lane >= o) incl += v;
-        }
-        const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
-        int wpos = incl - cnt;
-        uint32_t f = flagged;
-        while (f) {
-          const int col = __ffs(static_cast<int>(f)) - 1;
-          f &= f - 1;
-          queue[wpos++] = static_cast<uint32_t>((row << 8) | col);
-        }
-        __syncwarp();
-        for (int i = lane; i < total; i += 32) {
-          const uint32_t e = queue[i];
-          const int r = static_cast<int>(e >> 8), c = static_cast<int>(e & 0xFF);
-          const uint16_t* xr = p.x + static_cast<int64_t>(m0 + r) * p.K;
-          double acc64 = 0.0;
-          for (int kb = 0; kb < KB; ++kb) {
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-              const uint4 av = __ldg(reinterpret_cast<const uint4*>(xr + kb * 64 + ch * 8));
-              const uint4 bv =
-                  *reinterpret_cast<const uint4*>(b_smem + kb * kWBBox + sw128_off(c, ch));
-              const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                acc64 = fma(static_cast<double>(bf16lo_to_f32(aw[q])),
-                            static_cast<double>(bf16lo_to_f32(bw[q])), acc64);
-                acc64 = fma(static_cast<double>(bf16hi_to_f32(aw[q])),
-                            static_cast<double>(bf16hi_to_f32(bw[q])), acc64);
-              }
-            }
-          }
-          queue[i] = (e & 0xFFFFu) | (round_f64_to_bf16(acc64) << 16);
-        }
-        __syncwarp();
-        for (int i = 0; i < total; ++i) {
-          const uint32_t e = queue[i];
-          if (static_cast<int>((e >> 8) & 0xFF) == row) {
-            const uint32_t c = e & 0xFFu;
-#pragma unroll
-            for (int j = 0; j < kWBN; ++j)
-              if (static_cast<uint32_t>(j) == c) bits[j] = e >> 16;
-          }
-        }
-        __syncwarp();
-        if (row_valid) {
-          uint32_t o[kWBN / 2];
-#pragma unroll
-          for (int i = 0; i < kWBN; i += 2) {
-            const uint32_t lo = f32_to_bf16_rne(__fmul_rn(__uint_as_float(bits[i] << 16), p.scale));
-            const uint32_t hi =
-                f32_to_bf16_rne(__fmul_rn(__uint_as_float(bits[i + 1] << 16), p.scale));
-            o[i >> 1] = lo | (hi << 16);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(p.w_out + static_cast<int64_t>(m0 + row) * kWBN);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
-      }
-      if (!named_bar_and(1, 128, ok)) break;
-    }
-  }
-
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
-  }
-}
-
 int set_smem_attr(const void* fn, int bytes, bool* done, int dev) {
   if (done[dev]) return DSA_OK;
   const int st = cuda_status(
@@ -1052,50 +746,6 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
   const int64_t fblocks = (rows + kFixWarps - 1) / kFixWarps;
   const int64_t fgrid = fblocks < 8 * di.num_sms ? fblocks : 8 * di.num_sms;
   qproj_fixup_kernel<<<static_cast<unsigned>(fgrid), kFixWarps * 32, 0, stream>>>(f);
-  return cuda_status(cudaGetLastError());
-}
-
-int launch_wproj(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
-                 cudaStream_t stream) {
-  using namespace ixp;
-  DeviceInfo di;
-  int st = current_device_info(&di);
-  if (st != DSA_OK) return st;
-  if (di.max_smem_optin < kWSmem) return DSA_ERR_UNSUPPORTED;
-  unsigned int* err = nullptr;
-  st = device_error_word(&err);
-  if (st != DSA_OK) return st;
-  CUtensorMap tm_a, tm_b;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {64, kBM};
-    st = encode_tensor_map(&tm_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st != DSA_OK) return st;
-  }
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(kWBN)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-    const uint32_t box[2] = {64, kWBN};
-    st = encode_tensor_map(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wp, dims, strides, box,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st != DSA_OK) return st;
-  }
-  WParams p;
-  p.M = static_cast<int>(rows);
-  p.K = K;
-  p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
-  p.gamma = gamma_for(K / kKC);
-  p.scale = scale;
-  p.x = static_cast<const uint16_t*>(x);
-  p.w_out = static_cast<uint16_t*>(w_out);
-  p.err = err;
-  static bool attr_done[64] = {false};
-  st = set_smem_attr(reinterpret_cast<const void*>(wproj_kernel), kWSmem, attr_done, di.device);
-  if (st != DSA_OK) return st;
-  const int grid = p.m_tiles < di.num_sms ? p.m_tiles : di.num_sms;
-  wproj_kernel<<<grid, kWThreads, kWSmem, stream>>>(tm_a, tm_b, p);
   return cuda_status(cudaGetLastError());
 }
 
