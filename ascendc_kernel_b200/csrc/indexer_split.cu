@@ -53,27 +53,29 @@ __global__ void row_split_s8_kernel(const uint16_t* __restrict__ src, int64_t ro
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  uint32_t w[NC][4];
-#pragma unroll
-  for (int j = 0; j < NC; ++j) {
+  // each pass reads the row again (the second read hits L1), so that no chunk
+  // has to stay in registers between the passes
+  auto load = [&](int j, uint32_t (&w)[4]) {
     const int c = j * 256 + lane * 8;
-    w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0u;
+    w[0] = w[1] = w[2] = w[3] = 0u;
     if (c < K) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + row * K + c));
-      w[j][0] = v.x, w[j][1] = v.y, w[j][2] = v.z, w[j][3] = v.w;
+      w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
     }
-  }
+  };
   // sigma: max over elements of (leading bit + 1); non-finite marks the row
   int top = -(1 << 30);
   int low = 1 << 30;  // lowest set bit position of a nonzero element
   bool finite = true;
 #pragma unroll
   for (int j = 0; j < NC; ++j) {
+    uint32_t w[4];
+    load(j, w);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t b = (w[j][q] >> (16 * h)) & 0xFFFFu;
+        const uint32_t b = (w[q] >> (16 * h)) & 0xFFFFu;
         finite &= ((b >> 7) & 0xFFu) != 0xFFu;
         top = max(top, bf16_top(b));
         const uint32_t e = (b >> 7) & 0xFFu, m = b & 0x7Fu;
@@ -95,12 +97,14 @@ __global__ void row_split_s8_kernel(const uint16_t* __restrict__ src, int64_t ro
   const int64_t plane = rows * K;
 #pragma unroll
   for (int j = 0; j < NC; ++j) {
+    uint32_t w[4];
+    load(j, w);
     uint32_t s[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t b = (w[j][q] >> (16 * h)) & 0xFFFFu;
+        const uint32_t b = (w[q] >> (16 * h)) & 0xFFFFu;
         const uint32_t e = (b >> 7) & 0xFFu, m = b & 0x7Fu;
         const uint32_t M = e ? (m | 0x80u) : m;
         const int eb = e ? static_cast<int>(e) : 1;
