@@ -34,6 +34,20 @@
 namespace dsa {
 namespace ixw {
 
+// Lowest set bit position (value 2^pos) over the two bf16 of a word; 1 << 30
+// when both are zero.
+__device__ __forceinline__ int bf16x2_low_bit(uint32_t w) {
+  int low = 1 << 30;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t b = (w >> (16 * h)) & 0x7FFFu;
+    const uint32_t e = b >> 7, m = b & 0x7Fu;
+    const uint32_t M = e ? (m | 0x80u) : m;
+    if (M) low = min(low, (e ? static_cast<int>(e) : 1) - 134 + (__ffs(M) - 1));
+  }
+  return low;
+}
+
 constexpr int kBM = 128;
 constexpr int kBN = 16;
 constexpr int kMaxK = 1024;
@@ -66,8 +80,7 @@ struct Params {
   const int* b_sig;     // [16]
   const float* b_err;   // [16]
   const float* b_n3;    // [16]
-  const int* a_span;    // [M] bit spans (indexer_split.cu)
-  const int* b_span;    // [16]
+  const int* b_span;    // [16] bit spans (indexer_split.cu)
   const uint16_t* x;    // bf16 [M, K], for the exact recomputation
   const uint16_t* wp;   // bf16 [16, K]
   uint16_t* w_out;      // bf16 [M, 16]
@@ -298,17 +311,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = static_cast<int>(e >> 8), c = static_cast<int>(e & 0xFF);
           const uint16_t* xr = p.x + static_cast<int64_t>(m0 + r) * p.K;
           const uint16_t* wr = p.wp + static_cast<int64_t>(c) * p.K;
-          const bool any_order = __ldg(p.a_span + m0 + r) + __ldg(p.b_span + c) + log2k <= 53;
+          // the x row's span (sigma - lowest set bit), from the lanes' slices of k
+          const int k0 = lane * 32;
+          uint4 av[4], bv[4];
+          int low = 1 << 30;
+          if (k0 < p.K) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              av[j] = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8 * j));
+              bv[j] = __ldg(reinterpret_cast<const uint4*>(wr + k0 + 8 * j));
+              low = min(low, min(min(bf16x2_low_bit(av[j].x), bf16x2_low_bit(av[j].y)),
+                                 min(bf16x2_low_bit(av[j].z), bf16x2_low_bit(av[j].w))));
+            }
+          }
+          low = __reduce_min_sync(0xFFFFFFFFu, low);
+          const int sg = __ldg(p.a_sig + m0 + r);
+          const int a_span = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
+          const bool any_order = a_span + __ldg(p.b_span + c) + log2k <= 53;
           double acc64 = 0.0;
           if (any_order) {
-            const int k0 = lane * 32;
             if (k0 < p.K) {
-              uint4 av[4], bv[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                av[j] = __ldg(reinterpret_cast<const uint4*>(xr + k0 + 8 * j));
-                bv[j] = __ldg(reinterpret_cast<const uint4*>(wr + k0 + 8 * j));
-              }
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const uint32_t aw[4] = {av[j].x, av[j].y, av[j].z, av[j].w};
@@ -387,7 +409,7 @@ int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* si
 size_t wproj_s8_scratch_bytes(int64_t rows, int K) {
   auto a256 = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
   const size_t R = static_cast<size_t>(rows), Kz = static_cast<size_t>(K);
-  return a256(3 * R * Kz) + 4 * a256(R * 4) + a256(3 * 16 * Kz) + 4 * a256(16 * 4);
+  return a256(3 * R * Kz) + 3 * a256(R * 4) + a256(3 * 16 * Kz) + 4 * a256(16 * 4);
 }
 
 int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
@@ -413,8 +435,6 @@ int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, in
   ws += a256(R * 4);
   float* a_n3 = reinterpret_cast<float*>(ws);
   ws += a256(R * 4);
-  int* a_span = reinterpret_cast<int*>(ws);
-  ws += a256(R * 4);
   int8_t* b_sl = reinterpret_cast<int8_t*>(ws);
   ws += a256(3 * 16 * Kz);
   int* b_sig = reinterpret_cast<int*>(ws);
@@ -426,7 +446,7 @@ int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, in
   int* b_span = reinterpret_cast<int*>(ws);
   st = launch_row_split(wp, kBN, K, b_sl, b_sig, b_err, b_n3, b_span, stream);
   if (st != DSA_OK) return st;
-  st = launch_row_split(x, rows, K, a_sl, a_sig, a_err, a_n3, a_span, stream);
+  st = launch_row_split(x, rows, K, a_sl, a_sig, a_err, a_n3, nullptr, stream);
   if (st != DSA_OK) return st;
   CUtensorMap tm_a, tm_b;
   {
@@ -456,7 +476,6 @@ int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, in
   p.b_sig = b_sig;
   p.b_err = b_err;
   p.b_n3 = b_n3;
-  p.a_span = a_span;
   p.b_span = b_span;
   p.x = static_cast<const uint16_t*>(x);
   p.wp = static_cast<const uint16_t*>(wp);
