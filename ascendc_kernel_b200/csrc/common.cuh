@@ -447,6 +447,16 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_add_rm(uint64_t a, uint64_t b) {  // rounded down
+  uint64_t d;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma_rp(uint64_t a, uint64_t b, uint64_t c) {  // rounded up
+  uint64_t d;
+  asm("fma.rp.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 // max of three floats in one instruction
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

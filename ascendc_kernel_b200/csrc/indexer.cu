@@ -8,10 +8,12 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
                       void* q_out, int64_t rows, int K, int n_heads, int rope_dim, int64_t seqlen,
                       const void* a_slices, const int* a_sig, const float* a_err,
                       const float* a_n3, const void* b_slices, const int* b_sig,
-                      const float* b_err, const float* b_n3, const int* a_span,
-                      const int* b_span, uint32_t* open_bits, cudaStream_t stream);
-int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* sig, float* err,
-                     float* n3, int* span, cudaStream_t stream);
+                      const float* b_err, const float* b_n3, const int* b_span,
+                      uint32_t* open_bits, cudaStream_t stream);
+int launch_row_split2(const void* a_src, int64_t a_rows, void* a_slices, int* a_sig,
+                      float* a_err, float* a_n3, int* a_span, const void* b_src, int64_t b_rows,
+                      void* b_slices, int* b_sig, float* b_err, float* b_n3, int* b_span, int K,
+                      cudaStream_t stream);
 int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, int K, float scale,
                     void* scratch, cudaStream_t stream);
 size_t wproj_s8_scratch_bytes(int64_t rows, int K);
@@ -35,10 +37,10 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // Front part of the workspace: the int8 slices of wq_b and of qr for the q
 // projection (indexer_split.cu), 3 planes each, sized for q_lora_rank <= 256,
-// with the per-row exponent, remainder bound, ||S3|| and bit span, and the
-// bitmask of output elements left to the exact fix-up.
+// with the per-row exponent, remainder bound and ||S3|| (and the bit span of
+// the wq_b rows), and the bitmask of output elements left to the exact fix-up.
 struct SliceRegion {
-  size_t b_slices, b_sig, b_err, b_n3, b_span, a_slices, a_sig, a_err, a_n3, a_span, open, bytes;
+  size_t b_slices, b_sig, b_err, b_n3, b_span, a_slices, a_sig, a_err, a_n3, open, bytes;
 };
 constexpr size_t kMaxQLora = 256;
 SliceRegion slice_region(int n_heads, int head_dim, int64_t rows) {
@@ -54,8 +56,7 @@ SliceRegion slice_region(int n_heads, int head_dim, int64_t rows) {
   r.a_sig = r.a_slices + align256(3 * R * kMaxQLora);
   r.a_err = r.a_sig + align256(R * 4);
   r.a_n3 = r.a_err + align256(R * 4);
-  r.a_span = r.a_n3 + align256(R * 4);
-  r.open = r.a_span + align256(R * 4);
+  r.open = r.a_n3 + align256(R * 4);
   r.bytes = r.open + align256(R * (N / 8));
   return r;
 }
@@ -81,15 +82,14 @@ int run_qproj(const void* qr, const void* wq, const float* cos_tab, const float*
   float* a_err = reinterpret_cast<float*>(ws + r.a_err);
   float* a_n3 = reinterpret_cast<float*>(ws + r.a_n3);
   int* b_span = reinterpret_cast<int*>(ws + r.b_span);
-  int* a_span = reinterpret_cast<int*>(ws + r.a_span);
-  int st = launch_row_split(wq, static_cast<int64_t>(n_heads) * head_dim, K, ws + r.b_slices,
-                            b_sig, b_err, b_n3, b_span, s);
-  if (st == DSA_OK)
-    st = launch_row_split(qr, rows, K, ws + r.a_slices, a_sig, a_err, a_n3, a_span, s);
+  // wq_b rows (with bit spans, for the exact fix-up) and qr rows in one launch
+  const int st = launch_row_split2(wq, static_cast<int64_t>(n_heads) * head_dim, ws + r.b_slices,
+                                   b_sig, b_err, b_n3, b_span, qr, rows, ws + r.a_slices, a_sig,
+                                   a_err, a_n3, nullptr, K, s);
   if (st != DSA_OK) return st;
   return launch_qproj_rope(qr, wq, cos_tab, sin_tab, q_out, rows, K, n_heads, rope_dim, seqlen,
                            ws + r.a_slices, a_sig, a_err, a_n3, ws + r.b_slices, b_sig, b_err,
-                           b_n3, a_span, b_span, reinterpret_cast<uint32_t*>(ws + r.open), s);
+                           b_n3, b_span, reinterpret_cast<uint32_t*>(ws + r.open), s);
 }
 
 int check_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,

@@ -486,7 +486,7 @@ struct FixParams {
   int64_t seqlen;
   const uint16_t* qr;     // [M, K]
   const uint16_t* wq;     // [N, K]
-  const int* a_span;      // [M]
+  const int* a_sig;       // [M] row exponents (indexer_split.cu)
   const int* b_span;      // [N]
   const float* cos_tab;
   const float* sin_tab;
@@ -574,7 +574,16 @@ __global__ void __launch_bounds__(kFixWarps * 32)
         if (lane * 8 < p.K)
           a[lane] = __ldg(reinterpret_cast<const uint4*>(p.qr + static_cast<int64_t>(row) * p.K) +
                           lane);
-        span_a = __ldg(p.a_span + row);
+        // the row's bit span (sigma - lowest set bit), from the staged row
+        int low = 1 << 30;
+        if (lane * 8 < p.K) {
+          const uint4 v = a[lane];
+          low = min(min(bf16x2_low_bit(v.x), bf16x2_low_bit(v.y)),
+                    min(bf16x2_low_bit(v.z), bf16x2_low_bit(v.w)));
+        }
+        low = __reduce_min_sync(0xFFFFFFFFu, low);
+        const int sg = __ldg(p.a_sig + row);
+        span_a = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
         staged = true;
         __syncwarp();
       }
@@ -654,8 +663,8 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
                       void* q_out, int64_t rows, int K, int n_heads, int rope_dim, int64_t seqlen,
                       const void* a_slices, const int* a_sig, const float* a_err,
                       const float* a_n3, const void* b_slices, const int* b_sig,
-                      const float* b_err, const float* b_n3, const int* a_span,
-                      const int* b_span, uint32_t* open_bits, cudaStream_t stream) {
+                      const float* b_err, const float* b_n3, const int* b_span,
+                      uint32_t* open_bits, cudaStream_t stream) {
   using namespace ixp;
   DeviceInfo di;
   int st = current_device_info(&di);
@@ -728,7 +737,7 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
   f.seqlen = seqlen;
   f.qr = static_cast<const uint16_t*>(qr);
   f.wq = static_cast<const uint16_t*>(wq);
-  f.a_span = a_span;
+  f.a_sig = a_sig;
   f.b_span = b_span;
   f.cos_tab = cos_tab;
   f.sin_tab = sin_tab;

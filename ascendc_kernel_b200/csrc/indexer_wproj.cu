@@ -34,20 +34,6 @@
 namespace dsa {
 namespace ixw {
 
-// Lowest set bit position (value 2^pos) over the two bf16 of a word; 1 << 30
-// when both are zero.
-__device__ __forceinline__ int bf16x2_low_bit(uint32_t w) {
-  int low = 1 << 30;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t b = (w >> (16 * h)) & 0x7FFFu;
-    const uint32_t e = b >> 7, m = b & 0x7Fu;
-    const uint32_t M = e ? (m | 0x80u) : m;
-    if (M) low = min(low, (e ? static_cast<int>(e) : 1) - 134 + (__ffs(M) - 1));
-  }
-  return low;
-}
-
 constexpr int kBM = 128;
 constexpr int kBN = 16;
 constexpr int kMaxK = 1024;
@@ -402,8 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace ixw
 
-int launch_row_split(const void* src, int64_t rows, int K, void* slices, int* sig, float* err,
-                     float* n3, int* span, cudaStream_t stream);
+int launch_row_split2(const void* a_src, int64_t a_rows, void* a_slices, int* a_sig,
+                      float* a_err, float* a_n3, int* a_span, const void* b_src, int64_t b_rows,
+                      void* b_slices, int* b_sig, float* b_err, float* b_n3, int* b_span, int K,
+                      cudaStream_t stream);
 
 // Scratch the sliced w projection needs (256-byte aligned pieces).
 size_t wproj_s8_scratch_bytes(int64_t rows, int K) {
@@ -444,9 +432,9 @@ int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, in
   float* b_n3 = reinterpret_cast<float*>(ws);
   ws += a256(16 * 4);
   int* b_span = reinterpret_cast<int*>(ws);
-  st = launch_row_split(wp, kBN, K, b_sl, b_sig, b_err, b_n3, b_span, stream);
-  if (st != DSA_OK) return st;
-  st = launch_row_split(x, rows, K, a_sl, a_sig, a_err, a_n3, nullptr, stream);
+  // w_proj rows (with bit spans, for the exact fix-up) and x rows in one launch
+  st = launch_row_split2(wp, kBN, b_sl, b_sig, b_err, b_n3, b_span, x, rows, a_sl, a_sig, a_err,
+                         a_n3, nullptr, K, stream);
   if (st != DSA_OK) return st;
   CUtensorMap tm_a, tm_b;
   {

@@ -61,4 +61,18 @@ __device__ __forceinline__ float norm_upper(float ss, int n) {
 __device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Lowest set bit position (value 2^pos) over the two bf16 of a word; 1 << 30
+// when both are zero.
+__device__ __forceinline__ int bf16x2_low_bit(uint32_t w) {
+  int low = 1 << 30;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t b = (w >> (16 * h)) & 0x7FFFu;
+    const uint32_t e = b >> 7, m = b & 0x7Fu;
+    const uint32_t M = e ? (m | 0x80u) : m;
+    if (M) low = min(low, (e ? static_cast<int>(e) : 1) - 134 + (__ffs(M) - 1));
+  }
+  return low;
+}
+
 }  // namespace dsa

@@ -478,13 +478,21 @@ def run_profile_case(args):
         print(json.dumps({"profile_case": "ix", "batch": 8, "launches":
                           3 * (args.warmup + args.steps)}))
         return
-    if args.profile == "chain":
+    if args.profile in ("chain", "fchain"):
         # configs[3] at batch args.batch (1: ~0.9 GB on the device): indexer top-2048,
-        # then the long-pool SparseAttention over its indices
+        # then the long-pool SparseAttention over its indices ("chain": two calls,
+        # "fchain": the fused dsa_chain_fwd call)
         model, x, qr, q, pool, sink = make_chain_case(dev, args.batch)
         out = torch.empty_like(q)
-        for _ in range(args.warmup + args.steps):
-            sa.sparse_attn(q, pool, sink, model(x, qr, 0, 0), 128 ** -0.5, out=out)
+        if args.profile == "fchain":
+            from ascendc_kernel_b200 import chain
+
+            sam = sa.ModelNew(q.shape[2], q.shape[3]).to(dev)
+            for _ in range(args.warmup + args.steps):
+                chain.indexer_sparse_attn(model, sam, x, qr, 0, 0, q, pool, out=out)
+        else:
+            for _ in range(args.warmup + args.steps):
+                sa.sparse_attn(q, pool, sink, model(x, qr, 0, 0), 128 ** -0.5, out=out)
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": "chain", "batch": args.batch,
                           "steps": args.warmup + args.steps}))
@@ -510,7 +518,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa", "ix", "chain"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix", "chain", "fchain"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()

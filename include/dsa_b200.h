@@ -186,7 +186,7 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
  * operand slices and the q and w intermediates live in a fixed 128 MiB array inside the library, one per
  * device that loads it, held until the process exits. The request needs
  * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
- * <= 128 MiB, i.e. at most 25,961 tokens (batch*seqlen) at 16 heads x 64 dims
+ * <= 128 MiB, i.e. at most 25,981 tokens (batch*seqlen) at 16 heads x 64 dims
  * with n_cand <= 1024 and topk <= 256 (fewer with a score buffer); larger
  * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
  * device looks up the array's address; make it before any stream capture.
