@@ -457,6 +457,25 @@ __device__ __forceinline__ uint64_t f2_fma_rp(uint64_t a, uint64_t b, uint64_t c
   asm("fma.rp.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_fma_rm(uint64_t a, uint64_t b, uint64_t c) {  // rounded down
+  uint64_t d;
+  asm("fma.rm.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// acc + the low (high) bf16 of w, converted exactly, the sum rounded down (up):
+// one mixed-precision add, no separate conversion
+__device__ __forceinline__ float add_rd_bf16lo(uint32_t w, float acc) {
+  float d;
+  asm("{.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rm.f32.bf16 %0, l, %2;}"
+      : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float add_ru_bf16hi(uint32_t w, float acc) {
+  float d;
+  asm("{.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rp.f32.bf16 %0, h, %2;}"
+      : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
 // max of three floats in one instruction
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

@@ -549,6 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
           tc_fence_after();
           const float kvn = row_norm64(kvs, row) * kGamma;
+          const uint64_t kv2 = f2_pack(kvn, kvn), nkv2 = f2_pack(-kvn, -kvn);
           const uint32_t* wpk = reinterpret_cast<const uint32_t*>(smem + kOffWP);
           const uint32_t* psel = reinterpret_cast<const uint32_t*>(smem + kOffPS);
 #pragma unroll 1
@@ -561,10 +562,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 2; ++j) {
               const int tt = tt0 + j;
               const bool active = k < nvs[tt];
-              // Each head score s_h is known to lie in [v - E, v + E]; carry the
-              // interval [RNE(v-E), RNE(v+E)] through relu, *w (bf16 RNE, both
-              // monotone) and the head sum (fp32, rounded outward). If both ends
-              // of the sum round to the same bf16, that is the exact score.
+              // Each head score s_h is known to lie in [v - E, v + E] (E = q_h's
+              // norm bound times kvn); carry the interval [RNE(v-E), RNE(v+E)]
+              // through relu, *w (bf16 RNE, both monotone) and the head sum
+              // (fp32, rounded outward). If both ends of the sum round to the
+              // same bf16, that is the exact score. The ends v +- E come from
+              // one directed-rounding fma per two heads.
               float slo[4] = {0.f, 0.f, 0.f, 0.f}, shi[4] = {0.f, 0.f, 0.f, 0.f};
               uint32_t prs[16];
 #pragma unroll
@@ -572,24 +575,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float4 qv4 = reinterpret_cast<const float4*>(qn + tt * 16)[h4];
                 const uint4 wp4 = reinterpret_cast<const uint4*>(wpk + tt * 16)[h4];
                 const uint4 ps4 = reinterpret_cast<const uint4*>(psel + tt * 16)[h4];
-                const float qva[4] = {qv4.x, qv4.y, qv4.z, qv4.w};
+                const uint64_t qq[2] = {f2_pack(qv4.x, qv4.y), f2_pack(qv4.z, qv4.w)};
                 const uint32_t wpa[4] = {wp4.x, wp4.y, wp4.z, wp4.w};
                 const uint32_t psa[4] = {ps4.x, ps4.y, ps4.z, ps4.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const int h = h4 * 4 + i;
-                  const float v = __uint_as_float(r[j * 16 + h]);
-                  const float E = __fmul_ru(qva[i], kvn);
-                  uint32_t pr;  // upper half RNE(v+E), lower half RNE(v-E)
-                  asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
-                      : "=r"(pr)
-                      : "f"(__fadd_ru(v, E)), "f"(__fsub_rd(v, E)));
-                  prs[h] = pr;
-                  uint32_t e2 = __byte_perm(pr, 0, psa[i]);
-                  asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
-                  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
-                  slo[i] = __fadd_rd(slo[i], bf16lo_to_f32(e2));
-                  shi[i] = __fadd_ru(shi[i], bf16hi_to_f32(e2));
+                for (int hp = 0; hp < 2; ++hp) {
+                  const int h = h4 * 4 + hp * 2;
+                  const uint64_t v2 = f2_pack(__uint_as_float(r[j * 16 + h]),
+                                              __uint_as_float(r[j * 16 + h + 1]));
+                  float hv[2], lv[2];
+                  f2_unpack(f2_fma_rp(qq[hp], kv2, v2), hv[0], hv[1]);
+                  f2_unpack(f2_fma_rm(qq[hp], nkv2, v2), lv[0], lv[1]);
+#pragma unroll
+                  for (int m = 0; m < 2; ++m) {
+                    const int i = hp * 2 + m;
+                    uint32_t pr;  // upper half RNE(v+E), lower half RNE(v-E)
+                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(hv[m]), "f"(lv[m]));
+                    prs[h + m] = pr;
+                    uint32_t e2 = __byte_perm(pr, 0, psa[i]);
+                    asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
+                    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
+                    slo[i] = add_rd_bf16lo(e2, slo[i]);
+                    shi[i] = add_ru_bf16hi(e2, shi[i]);
+                  }
                 }
               }
               const float lo_sum = __fadd_rd(__fadd_rd(slo[0], slo[1]), __fadd_rd(slo[2], slo[3]));
