@@ -476,6 +476,34 @@ __device__ __forceinline__ float add_ru_bf16hi(uint32_t w, float acc) {
       : "=f"(d) : "r"(w), "f"(acc));
   return d;
 }
+__device__ __forceinline__ float add_rd_bf16hi(uint32_t w, float acc) {
+  float d;
+  asm("{.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rm.f32.bf16 %0, h, %2;}"
+      : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float add_ru_bf16lo(uint32_t w, float acc) {
+  float d;
+  asm("{.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rp.f32.bf16 %0, l, %2;}"
+      : "=f"(d) : "r"(w), "f"(acc));
+  return d;
+}
+// Products of the low (high) bf16 halves of a and b: exact in fp32 up to
+// underflow (8 x 8 significand bits), without separate conversions.
+__device__ __forceinline__ float mul_bf16lo(uint32_t a, uint32_t b) {
+  float d;
+  asm("{.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %3;}"
+      : "=f"(d) : "r"(a), "r"(b), "f"(-0.0f));
+  return d;
+}
+__device__ __forceinline__ float mul_bf16hi(uint32_t a, uint32_t b) {
+  float d;
+  asm("{.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, ah, bh, %3;}"
+      : "=f"(d) : "r"(a), "r"(b), "f"(-0.0f));
+  return d;
+}
 // max of three floats in one instruction
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

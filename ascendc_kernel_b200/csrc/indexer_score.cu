@@ -145,8 +145,8 @@ __device__ __forceinline__ void load_token_vectors(const float* qn, const float*
 // Exact dot product of q row `qrow` and kv row `krow` (both SW128 in smem):
 // exact fp64 products summed in ascending dimension order (the oracle's
 // order), rounded once to bf16.
-__device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qrow,
-                                                   const uint8_t* kvbase, int krow) {
+__device__ __noinline__ uint32_t exact_dot_seq(const uint8_t* qbase, int qrow,
+                                               const uint8_t* kvbase, int krow) {
   double acc = 0.0;
 #pragma unroll
   for (int ch = 0; ch < 8; ++ch) {
@@ -165,11 +165,100 @@ __device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qro
   return round_f64_to_bf16(acc);
 }
 
+// The same bf16 value without fp64 conversions: the products of two bf16 are
+// exact in fp32 (up to underflow, below 2^-144 in total), and TwoSum chains
+// (Knuth; two of them, one per f32x2 lane) carry them as an unevaluated sum
+// s + c within 2^-30 sum|p| of the exact dot (compensated summation, Ogita,
+// Rump and Oishi 2005, with a wide margin); the oracle's sequential fp64 sum is
+// within 64 2^-53 sum|p| of it. sum|p| <= ||q|| ||kv|| <= bound / kGamma, so
+// the value is decided when the bf16 rounding agrees at both ends of
+// s + c -+ bound 2^-10; otherwise the sequential fp64 sum decides.
+// `bound` >= kGamma ||q|| ||kv||.
+__device__ __forceinline__ uint32_t exact_dot_bits(const uint8_t* qbase, int qrow,
+                                                   const uint8_t* kvbase, int krow, float bound) {
+  uint64_t s2 = f2_pack(0.f, 0.f), c2 = f2_pack(0.f, 0.f);
+#pragma unroll 2
+  for (int ch = 0; ch < 8; ++ch) {
+    const uint4 a = *reinterpret_cast<const uint4*>(qbase + sw128_off(qrow, ch));
+    const uint4 b = *reinterpret_cast<const uint4*>(kvbase + sw128_off(krow, ch));
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint64_t p2 = f2_pack(mul_bf16lo(aw[e], bw[e]), mul_bf16hi(aw[e], bw[e]));
+      const uint64_t t2 = f2_add(s2, p2);
+      const uint64_t bp2 = f2_sub(t2, s2);
+      const uint64_t e2 = f2_add(f2_sub(s2, f2_sub(t2, bp2)), f2_sub(p2, bp2));
+      s2 = t2;
+      c2 = f2_add(c2, e2);
+    }
+  }
+  float s0, s1, c0, c1;
+  f2_unpack(s2, s0, s1);
+  f2_unpack(c2, c0, c1);
+  const float t = __fadd_rn(s0, s1);
+  const float bp = __fsub_rn(t, s0);
+  const float c = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(__fsub_rn(s0, __fsub_rn(t, bp)),
+                                                        __fsub_rn(s1, bp)));
+  const float d = __fmaf_ru(bound, 0x1p-10f, 0x1p-140f);
+  if (isfinite(t) && isfinite(c) && isfinite(d)) {
+    const float lo = __fadd_rd(t, __fsub_rd(c, d)), hi = __fadd_ru(t, __fadd_ru(c, d));
+    const uint32_t blo = f32_to_bf16_rne(lo);
+    if (blo == f32_to_bf16_rne(hi)) return blo;
+  }
+  return exact_dot_seq(qbase, qrow, kvbase, krow);
+}
+
+// score_key over a queue entry's head scores (the low halves of words 1..16).
+__device__ __noinline__ uint32_t score_key_slow(const uint32_t* e, const float* wv, int k) {
+  uint32_t sb[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) sb[h] = e[1 + h] & 0xFFFFu;
+  float wf[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) wf[h] = wv[h];
+  return score_key(sb, wf, k);
+}
+
+// Score key of a drained pair from its 16 exact head scores (the low halves of
+// words 1..16 of the entry): e_h = bf16(relu(s_h) * w_h) two heads at a time
+// (bf16x2, RNE), their sum in fp32 rounded down and up; when both round to the
+// same bf16 that is the exact sum's rounding, otherwise the fp64 chain
+// (score_key) decides. wpk: per head {w, w} as bf16x2, wv: per head w.
+__device__ __forceinline__ uint32_t drained_key(const uint32_t* e, const uint32_t* wpk,
+                                                const float* wv, int k) {
+  float lo[2] = {0.f, 0.f}, hi[2] = {0.f, 0.f};
+#pragma unroll
+  for (int hp = 0; hp < 8; ++hp) {
+    uint32_t x = __byte_perm(e[1 + 2 * hp], e[2 + 2 * hp], 0x5410u);
+    const uint32_t w2 = __byte_perm(wpk[2 * hp], wpk[2 * hp + 1], 0x5410u);
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(x) : "r"(x), "r"(0u));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(x) : "r"(x), "r"(w2));
+    lo[hp & 1] = add_rd_bf16hi(x, add_rd_bf16lo(x, lo[hp & 1]));
+    hi[hp & 1] = add_ru_bf16hi(x, add_ru_bf16lo(x, hi[hp & 1]));
+  }
+  const float ls = __fadd_rd(lo[0], lo[1]), hs = __fadd_ru(hi[0], hi[1]);
+  if (isfinite(ls) && isfinite(hs)) {
+    uint32_t tp;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(tp) : "f"(hs), "f"(ls));
+    uint32_t tlo = tp & 0xFFFFu, thi = tp >> 16;
+    if (tlo == 0x8000u) tlo = 0;  // -0 == +0
+    if (thi == 0x8000u) thi = 0;
+    if (tlo == thi) {
+      const uint32_t ord = (tlo & 0x8000u) ? (~tlo & 0xFFFFu) : (tlo | 0x8000u);
+      return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+    }
+  }
+  return score_key_slow(e, wv, k);
+}
+
 // Per-warp queue of (token, candidate) pairs of the last one or two chunks
 // whose score could not be certified. Entry: word 0 = kv stage << 28 | token
 // slot << 16 | candidate k, words 1..16 = per head the bf16 pair {RNE(v+E),
-// RNE(v-E)} of the interval that holds the head's exact bf16 score.
-constexpr int kRqWords = 17;
+// RNE(v-E)} of the interval that holds the head's exact bf16 score, word 17 =
+// the kv row's norm bound times kGamma (19 words: an odd stride keeps the
+// lanes' reads of one word on distinct banks).
+constexpr int kRqWords = 19;
 
 __device__ __forceinline__ bool bf16_positive(uint32_t h16) {
   return h16 != 0u && !(h16 & 0x8000u);
@@ -183,9 +272,10 @@ __device__ __forceinline__ uint32_t ord_to_bf16(uint32_t ord) {
 // One lane per queued pair: exact recomputation of the heads whose interval is
 // open and can be positive, then the exact score chain; writes the key (or,
 // with gs, the bf16 score to gs[token slot * gld + k]).
-__device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
+__device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs, const float* qn,
                                          const uint8_t* kv_stages, const float* wv,
-                                         uint32_t* keys, uint16_t* gs, int64_t gld, int lane) {
+                                         const uint32_t* wpk, uint32_t* keys, uint16_t* gs,
+                                         int64_t gld, int lane) {
   __syncwarp();
   for (int i = lane; i < n; i += 32) {
     uint32_t* e = rq + i * kRqWords;
@@ -206,18 +296,11 @@ __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
     while (open) {
       const int h = __ffs(static_cast<int>(open)) - 1;
       open &= open - 1;
-      e[1 + h] = exact_dot_bits(qs, tt * 16 + h, kvs, row);
+      e[1 + h] = exact_dot_bits(qs, tt * 16 + h, kvs, row,
+                                qn[tt * 16 + h] * __uint_as_float(e[17]));
     }
-    uint32_t sb[16];
-#pragma unroll
-    for (int h = 0; h < 16; ++h) sb[h] = e[1 + h] & 0xFFFFu;  // certified, exact, or relu'd to 0
-    float wf[16];
-#pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) {
-      const float4 c = reinterpret_cast<const float4*>(wv + tt * 16)[h4];
-      wf[4 * h4 + 0] = c.x; wf[4 * h4 + 1] = c.y; wf[4 * h4 + 2] = c.z; wf[4 * h4 + 3] = c.w;
-    }
-    const uint32_t key = score_key(sb, wf, k);
+    // head scores now certified, exact, or relu'd to 0
+    const uint32_t key = drained_key(e, wpk + tt * 16, wv + tt * 16, k);
     if (gs)
       gs[tt * gld + k] = static_cast<uint16_t>(ord_to_bf16(key >> 16));
     else
@@ -611,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {
-                  drain_queue(rq, rq_n, qs, kv_stages, wv, keys, gs, p.score_ld, lane);
+                  drain_queue(rq, rq_n, qs, qn, kv_stages, wv, wpk, keys, gs, p.score_ld, lane);
                   rq_n = 0;
                 }
                 if (need) {
@@ -620,6 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          static_cast<uint32_t>(k);
 #pragma unroll
                   for (int h = 0; h < 16; ++h) e[1 + h] = prs[h];
+                  e[17] = __float_as_uint(kvn);
                 }
                 rq_n += __popc(bal);
               }
@@ -636,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(&acc_empty[ab]);
           if ((c & 1) || c == nch - 1) {
-            if (rq_n > 0) drain_queue(rq, rq_n, qs, kv_stages, wv, keys, gs, p.score_ld, lane);
+            if (rq_n > 0) drain_queue(rq, rq_n, qs, qn, kv_stages, wv, wpk, keys, gs, p.score_ld, lane);
             rq_n = 0;
           }
         }
