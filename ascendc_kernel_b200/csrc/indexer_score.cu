@@ -269,49 +269,79 @@ __device__ __forceinline__ uint32_t ord_to_bf16(uint32_t ord) {
   return (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
 }
 
-// One lane per queued pair: exact recomputation of the heads whose interval is
-// open and can be positive, then the exact score chain; writes the key (or,
-// with gs, the bf16 score to gs[token slot * gld + k]).
+// Queued pairs, 32 at a time: exact recomputation of the heads whose interval
+// is open and can be positive (spread one per lane), then the exact score
+// chain, one lane per pair; writes the key (or, with gs, the bf16 score to
+// gs[token slot * gld + k]).
 __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs, const float* qn,
                                          const uint8_t* kv_stages, const float* wv,
                                          const uint32_t* wpk, uint32_t* keys, uint16_t* gs,
                                          int64_t gld, int lane) {
   __syncwarp();
-  for (int i = lane; i < n; i += 32) {
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
     uint32_t* e = rq + i * kRqWords;
-    const int tt = static_cast<int>((e[0] >> 16) & 0xFFFu);
-    const int k = static_cast<int>(e[0] & 0xFFFFu);
-    const int row = k & (kChunk - 1);
-    const uint8_t* kvs = kv_stages + (e[0] >> 28) * kKVBytes;
     uint32_t open = 0;  // heads whose interval is open and can be positive
+    if (i < n) {
 #pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      const uint32_t pr = e[1 + h];
-      const uint32_t lo16 = pr & 0xFFFFu, hi16 = pr >> 16;
-      if (lo16 != hi16 && bf16_positive(hi16)) open |= 1u << h;
+      for (int h = 0; h < 16; ++h) {
+        const uint32_t pr = e[1 + h];
+        const uint32_t lo16 = pr & 0xFFFFu, hi16 = pr >> 16;
+        if (lo16 != hi16 && bf16_positive(hi16)) open |= 1u << h;
+      }
     }
-    // one rolled loop (a single copy of the exact dot in the code); the exact
-    // value replaces the interval in the entry
+    // the (entry, head) recomputations of these 32 entries are spread over the
+    // lanes, one per lane and round; the exact value replaces the interval
+    const int cnt = __popc(open);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
 #pragma unroll 1
-    while (open) {
-      const int h = __ffs(static_cast<int>(open)) - 1;
-      open &= open - 1;
-      e[1 + h] = exact_dot_bits(qs, tt * 16 + h, kvs, row,
-                                qn[tt * 16 + h] * __uint_as_float(e[17]));
+    for (int j0 = 0; j0 < total; j0 += 32) {
+      const int j = j0 + lane;
+      // owner: the first lane whose inclusive count exceeds j
+      int own = 0;
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1) {
+        const int v = __shfl_sync(0xFFFFFFFFu, incl, own + step - 1);
+        if (v <= j) own += step;
+      }
+      const int excl = __shfl_sync(0xFFFFFFFFu, incl - cnt, own);
+      const uint32_t om = __shfl_sync(0xFFFFFFFFu, open, own);
+      if (j < total) {
+        const int h = static_cast<int>(__fns(om, 0u, j - excl + 1));
+        uint32_t* eo = rq + (i0 + own) * kRqWords;
+        const uint32_t w0 = eo[0];
+        const int tt = static_cast<int>((w0 >> 16) & 0xFFFu);
+        const int row = static_cast<int>(w0 & 0xFFFFu) & (kChunk - 1);
+        eo[1 + h] = exact_dot_bits(qs, tt * 16 + h, kv_stages + (w0 >> 28) * kKVBytes, row,
+                                   qn[tt * 16 + h] * __uint_as_float(eo[17]));
+      }
     }
-    // head scores now certified, exact, or relu'd to 0
-    const uint32_t key = drained_key(e, wpk + tt * 16, wv + tt * 16, k);
-    if (gs)
-      gs[tt * gld + k] = static_cast<uint16_t>(ord_to_bf16(key >> 16));
-    else
-      keys[tt * kMaxT + k] = key;
+    __syncwarp();
+    if (i < n) {
+      // head scores now certified, exact, or relu'd to 0
+      const int tt = static_cast<int>((e[0] >> 16) & 0xFFFu);
+      const int k = static_cast<int>(e[0] & 0xFFFFu);
+      const uint32_t key = drained_key(e, wpk + tt * 16, wv + tt * 16, k);
+      if (gs)
+        gs[tt * gld + k] = static_cast<uint16_t>(ord_to_bf16(key >> 16));
+      else
+        keys[tt * kMaxT + k] = key;
+    }
   }
   __syncwarp();
 }
 
-// Descending bitonic sort of 32*R keys held as v[r] = element r*32 + lane.
+// Descending bitonic sorts of two tokens' 32*R keys, held as v[r] (u[r]) =
+// element r*32 + lane, interleaved (independent chains hide each other's
+// shuffle latency).
 template <int R>
-__device__ __forceinline__ void warp_bitonic_desc(uint32_t (&v)[R], int lane) {
+__device__ __forceinline__ void warp_bitonic_desc2(uint32_t (&v)[R], uint32_t (&u)[R], int lane) {
 #pragma unroll
   for (int size = 2; size <= 32 * R; size <<= 1) {
 #pragma unroll
@@ -322,12 +352,15 @@ __device__ __forceinline__ void warp_bitonic_desc(uint32_t (&v)[R], int lane) {
         for (int r = 0; r < R; ++r) {
           if ((r & rs) == 0) {
             const int i = r * 32 + lane;
-            const bool desc_block = (i & size) == 0;  // overall descending
-            const uint32_t a = v[r], b = v[r | rs];
-            const bool swap = desc_block ? (a < b) : (a > b);
-            if (swap) {
+            const bool desc_block = (i & size) == 0;
+            const uint32_t a = v[r], b = v[r | rs], c = u[r], d = u[r | rs];
+            if (desc_block ? (a < b) : (a > b)) {
               v[r] = b;
               v[r | rs] = a;
+            }
+            if (desc_block ? (c < d) : (c > d)) {
+              u[r] = d;
+              u[r | rs] = c;
             }
           }
         }
@@ -336,11 +369,10 @@ __device__ __forceinline__ void warp_bitonic_desc(uint32_t (&v)[R], int lane) {
         for (int r = 0; r < R; ++r) {
           const int i = r * 32 + lane;
           const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, v[r], stride);
-          const bool lower = (i & stride) == 0;
-          const bool desc_block = (i & size) == 0;
-          // in a descending block the lower index keeps the max
-          const bool keep_max = (lower == desc_block);
-          v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
+          const uint32_t q = __shfl_xor_sync(0xFFFFFFFFu, u[r], stride);
+          const bool keep_max = (((i & stride) == 0) == ((i & size) == 0));
+          v[r] = keep_max ? max(v[r], o) : min(v[r], o);
+          u[r] = keep_max ? max(u[r], q) : min(u[r], q);
         }
       }
     }
@@ -348,92 +380,118 @@ __device__ __forceinline__ void warp_bitonic_desc(uint32_t (&v)[R], int lane) {
 }
 
 template <int R>
-__device__ __forceinline__ void sort_and_store(const uint32_t* sel, int nsel, int K_out,
-                                               int64_t* out_row, int64_t offset, int lane) {
-  uint32_t v[R];
+__device__ __forceinline__ void sort_and_store2(const uint32_t* sel0, int nsel0, int64_t* out0,
+                                                const uint32_t* sel1, int nsel1, int64_t* out1,
+                                                int K_out, int64_t offset, int lane) {
+  uint32_t v[R], u[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = r * 32 + lane;
-    v[r] = i < nsel ? sel[i] : 0u;
+    v[r] = i < nsel0 ? sel0[i] : 0u;
+    u[r] = i < nsel1 ? sel1[i] : 0u;
   }
-  warp_bitonic_desc<R>(v, lane);
+  warp_bitonic_desc2<R>(v, u, lane);
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = r * 32 + lane;
     if (i < K_out) {
-      out_row[i] = i < nsel ? static_cast<int64_t>(0xFFFFu - (v[r] & 0xFFFFu)) + offset
+      out0[i] = i < nsel0 ? static_cast<int64_t>(0xFFFFu - (v[r] & 0xFFFFu)) + offset
+                          : static_cast<int64_t>(-1);
+      if (out1)
+        out1[i] = i < nsel1 ? static_cast<int64_t>(0xFFFFu - (u[r] & 0xFFFFu)) + offset
                             : static_cast<int64_t>(-1);
     }
   }
 }
 
-// Top-Ksel of the n keys in `keys` (smem, in candidate order) by one warp. A
-// key is (orderable score << 16) | (0xFFFF - k), so the order is score
-// descending, then k ascending. The keys are held in registers (key r*32+lane
-// in v[r]); a binary search over the 16 score bits finds the largest score thr
-// with at least Ksel keys scoring >= thr, and keys scoring exactly thr are
-// taken in k order (the order they are stored in) up to Ksel. The selected keys
-// are then compacted and sorted.
+// Top-Ksel of the n keys in `keys` (smem, in candidate order) by one warp, for
+// two tokens at once (their steps interleaved; the second may be absent:
+// n1 = 0, out1 = nullptr). A key is (orderable score << 16) | (0xFFFF - k), so
+// the order is score descending, then k ascending. The keys are held in
+// registers (key r*32+lane in v[r]); a binary search over the 16 score bits
+// finds the largest score thr with at least Ksel keys scoring >= thr, and keys
+// scoring exactly thr are taken in k order (the order they are stored in) up
+// to Ksel. The selected keys are then compacted and sorted.
 template <int R>
-__device__ __forceinline__ void warp_topk_r(const uint32_t* keys, int n, int K_out, uint32_t* sel,
-                                            int64_t* out_row, int64_t offset, int lane) {
-  const int ksel = n < K_out ? n : K_out;
+__device__ __forceinline__ void warp_topk2_r(const uint32_t* keys0, int n0, const uint32_t* keys1,
+                                             int n1, int K_out, uint32_t* sel0, uint32_t* sel1,
+                                             int64_t* out0, int64_t* out1, int64_t offset,
+                                             int lane) {
+  const int ksel0 = n0 < K_out ? n0 : K_out, ksel1 = n1 < K_out ? n1 : K_out;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  uint32_t v[R];
+  uint32_t v[R], u[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = r * 32 + lane;
-    v[r] = i < n ? keys[i] : 0u;  // a real key scores >= 1, padding scores 0
+    v[r] = i < n0 ? keys0[i] : 0u;  // a real key scores >= 1, padding scores 0
+    u[r] = i < n1 ? keys1[i] : 0u;
   }
-  const bool take_all = n <= ksel;
-  uint32_t thr = 0;
-  int need_ties = 0;
-  if (!take_all) {
+  const bool all0 = n0 <= ksel0, all1 = n1 <= ksel1;
+  uint32_t thr0 = 0, thr1 = 0;
+  int need0 = 0, need1 = 0;
+  if (!(all0 && all1)) {
     for (int bit = 15; bit >= 0; --bit) {
-      const uint32_t cand = (thr | (1u << bit)) << 16;
-      int c = 0;
+      const uint32_t cand0 = (thr0 | (1u << bit)) << 16, cand1 = (thr1 | (1u << bit)) << 16;
+      int c0 = 0, c1 = 0;
 #pragma unroll
-      for (int r = 0; r < R; ++r) c += v[r] >= cand ? 1 : 0;
-      c = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
-      if (c >= ksel) thr |= 1u << bit;
+      for (int r = 0; r < R; ++r) {
+        c0 += v[r] >= cand0 ? 1 : 0;
+        c1 += u[r] >= cand1 ? 1 : 0;
+      }
+      c0 = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c0)));
+      c1 = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c1)));
+      if (c0 >= ksel0) thr0 |= 1u << bit;
+      if (c1 >= ksel1) thr1 |= 1u << bit;
     }
-    const uint32_t above = (thr + 1) << 16;
-    int c = 0;
+    const uint32_t above0 = (thr0 + 1) << 16, above1 = (thr1 + 1) << 16;
+    int c0 = 0, c1 = 0;
 #pragma unroll
-    for (int r = 0; r < R; ++r) c += v[r] >= above ? 1 : 0;
-    need_ties = ksel - static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
+    for (int r = 0; r < R; ++r) {
+      c0 += v[r] >= above0 ? 1 : 0;
+      c1 += u[r] >= above1 ? 1 : 0;
+    }
+    need0 = ksel0 - static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c0)));
+    need1 = ksel1 - static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c1)));
   }
-  int base = 0, ties = 0;
+  int base0 = 0, ties0 = 0, base1 = 0, ties1 = 0;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const uint32_t k = v[r];
-    const uint32_t sc = k >> 16;
-    const bool valid = r * 32 + lane < n;
-    const bool tie = !take_all && valid && sc == thr;
-    const uint32_t tb = __ballot_sync(0xFFFFFFFFu, tie);
-    const bool take =
-        valid && (take_all || sc > thr || (tie && ties + __popc(tb & lt_mask) < need_ties));
-    ties += __popc(tb);
-    const uint32_t b = __ballot_sync(0xFFFFFFFFu, take);
-    if (take) sel[base + __popc(b & lt_mask)] = k;
-    base += __popc(b);
+    const bool valid0 = r * 32 + lane < n0, valid1 = r * 32 + lane < n1;
+    const uint32_t sc0 = v[r] >> 16, sc1 = u[r] >> 16;
+    const bool tie0 = !all0 && valid0 && sc0 == thr0, tie1 = !all1 && valid1 && sc1 == thr1;
+    const uint32_t tb0 = __ballot_sync(0xFFFFFFFFu, tie0), tb1 = __ballot_sync(0xFFFFFFFFu, tie1);
+    const bool take0 =
+        valid0 && (all0 || sc0 > thr0 || (tie0 && ties0 + __popc(tb0 & lt_mask) < need0));
+    const bool take1 =
+        valid1 && (all1 || sc1 > thr1 || (tie1 && ties1 + __popc(tb1 & lt_mask) < need1));
+    ties0 += __popc(tb0);
+    ties1 += __popc(tb1);
+    const uint32_t b0 = __ballot_sync(0xFFFFFFFFu, take0), b1 = __ballot_sync(0xFFFFFFFFu, take1);
+    if (take0) sel0[base0 + __popc(b0 & lt_mask)] = v[r];
+    if (take1) sel1[base1 + __popc(b1 & lt_mask)] = u[r];
+    base0 += __popc(b0);
+    base1 += __popc(b1);
   }
   __syncwarp();
   if (K_out <= 128)
-    sort_and_store<4>(sel, base, K_out, out_row, offset, lane);
+    sort_and_store2<4>(sel0, base0, out0, sel1, base1, out1, K_out, offset, lane);
   else
-    sort_and_store<8>(sel, base, K_out, out_row, offset, lane);
+    sort_and_store2<8>(sel0, base0, out0, sel1, base1, out1, K_out, offset, lane);
   __syncwarp();
 }
 
-__device__ void warp_topk(const uint32_t* keys, int n, int K_out, uint32_t* sel, int64_t* out_row,
-                          int64_t offset, int lane) {
+__device__ void warp_topk2(const uint32_t* keys0, int n0, const uint32_t* keys1, int n1, int K_out,
+                           uint32_t* sel0, uint32_t* sel1, int64_t* out0, int64_t* out1,
+                           int64_t offset, int lane) {
+  const int n = n0 > n1 ? n0 : n1;
   if (n <= 256)
-    warp_topk_r<8>(keys, n, K_out, sel, out_row, offset, lane);
+    warp_topk2_r<8>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
   else if (n <= 512)
-    warp_topk_r<16>(keys, n, K_out, sel, out_row, offset, lane);
+    warp_topk2_r<16>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
+  else if (n <= 768)
+    warp_topk2_r<24>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
   else
-    warp_topk_r<32>(keys, n, K_out, sel, out_row, offset, lane);
+    warp_topk2_r<32>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -745,12 +803,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // all keys of the unit are written
       if (!named_bar_and(3, 256, ok)) break;
-      for (int tt = ew * 2; tt < ew * 2 + 2; ++tt) {
+      {
+        // the warp's two tokens, selected together (the second may lie past the end)
+        const int tt = ew * 2;
         const int64_t tok = t0 + tt;
-        if (tok >= p.S) continue;
-        const int64_t nv = n_valid(p, tok);
-        int64_t* out_row = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
-        warp_topk(keys + tt * kMaxT, static_cast<int>(nv), p.K, sel, out_row, p.offset, lane);
+        if (tok < p.S) {
+          const bool two = tok + 1 < p.S;
+          int64_t* out0 = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
+          warp_topk2(keys + tt * kMaxT, static_cast<int>(n_valid(p, tok)), keys + (tt + 1) * kMaxT,
+                     two ? static_cast<int>(n_valid(p, tok + 1)) : 0, p.K, sel, hist,
+                     out0, two ? out0 + p.K : nullptr, p.offset, lane);
+        }
       }
       if (!named_bar_and(3, 256, ok)) break;
     }
