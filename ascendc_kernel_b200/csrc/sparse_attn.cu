@@ -11,8 +11,11 @@
 //
 // B200 mapping. A tile is 128 consecutive (token, head) rows of one batch
 // (128 / n_heads tokens). Per CTA (one per SM, persistent over tiles):
-//   warp 0       TMA producer: q tile (2 x 16 KB SW128 boxes), kv[b] (2 x 4 KB
-//                SW128 boxes) and the tile's top-k indices into a 4-deep ring.
+//   warp 0       TMA producer: q tile (2 x 16 KB SW128 boxes) and the tile's
+//                top-k indices into a 4-deep ring; kv[b] (2 x 4 KB SW128 boxes)
+//                into one of two kv slots whenever the batch changes. A ring
+//                stage is free once mm1 has read q and the epilogue has
+//                counted the indices, long before the tile's output is done.
 //   warp 1       TMEM allocator + single-thread tcgen05 issuer:
 //                  mm1  S[128 x 32]  = Q[128 x 128] . KV^T        (8 x K16)
 //                  mm2  O[128 x 128] = (P_hi + P_mid + P_lo) . KV (6 x K16)
@@ -21,12 +24,13 @@
 //   warps 2..9   two epilogue warpgroups that own alternate tiles. Each
 //                thread owns one TMEM lane (= one (token, head) row): it reads
 //                its 32 scores, forms the multiplicity softmax with the sink
-//                logit, writes P to shared memory (K-major, no swizzle), waits
-//                for mm2, converts O to bf16 into the tile's q buffer (SW128
-//                layout, q is dead after mm1) and one thread TMA-stores it.
+//                logit, writes P to its shared-memory region (K-major, no
+//                swizzle), waits for mm2, converts O to bf16 into the same
+//                region (SW128 layout, P is dead after mm2) and one thread
+//                TMA-stores it.
 // TMEM: S[w] at columns [32w, 32w+32), O[w] at [128+128w, 256+128w); 512
-// columns allocated. q and out stream through HBM once; kv and the indices
-// are re-read from L2 per tile.
+// columns allocated. q and out stream through HBM once; the indices are read
+// once per tile, kv once per batch change.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -47,13 +51,15 @@ constexpr int kPPieces = 3;                 // hi, mid, lo
 constexpr int kThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 
+constexpr int kKVSlots = 2;
+constexpr int kPRegion = kQBytes;           // per warpgroup: P pieces, then the output tile
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + kStages * kQBytes;
-constexpr int kOffIdx = kOffKV + kStages * kKVBytes;
-constexpr int kOffP = kOffIdx + kStages * kIdxBytes;  // [2 wg][hi, mid, lo]
-constexpr int kOffCnt = kOffP + 2 * kPPieces * kPBytes;  // [2 wg][8 tokens][32] bytes
+constexpr int kOffIdx = kOffKV + kKVSlots * kKVBytes;
+constexpr int kOffP = kOffIdx + kStages * kIdxBytes;  // [2 wg][hi, mid, lo | out]
+constexpr int kOffCnt = kOffP + 2 * kPRegion;          // [2 wg][8 tokens][32] bytes
 constexpr int kOffBar = kOffCnt + 2 * 8 * 32;
-constexpr int kNumBars = 2 * kStages + 5 * 2 + 1;
+constexpr int kNumBars = 2 * kStages + 5 * 2 + kKVSlots + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + alignment slack
 
@@ -65,7 +71,7 @@ struct Params {
   int topk;
   int nkv;
   float scale_log2;  // softmax_scale * log2(e)
-  uint32_t tx_bytes;
+  uint32_t tx_bytes;  // q tile + indices of one stage
   const float* sink;
   unsigned int* err;
 };
@@ -82,13 +88,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;                  // [kStages] TMA -> MMA / epilogue
-  uint64_t* empty = bars + kStages;       // [kStages] epilogue (store read done) -> producer
+  uint64_t* empty = bars + kStages;       // [kStages] mm1 done + indices counted -> producer
   uint64_t* s_full = bars + 2 * kStages;  // [2] mm1 done -> epilogue w
   uint64_t* s_empty = s_full + 2;         // [2] S read -> MMA
   uint64_t* p_full = s_empty + 2;         // [2] P written -> MMA
   uint64_t* o_full = p_full + 2;          // [2] mm2 done -> epilogue w
   uint64_t* o_empty = o_full + 2;         // [2] O read -> MMA
-  uint64_t* drain_bar = o_empty + 2;      // MMA completion on teardown
+  uint64_t* kv_empty = o_empty + 2;       // [kKVSlots] last mm2 of a batch done -> producer
+  uint64_t* drain_bar = kv_empty + kKVSlots;  // MMA completion on teardown
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
 
@@ -98,8 +105,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 2);
     }
+    for (int k = 0; k < kKVSlots; ++k) mbar_init(&kv_empty[k], 1);
     for (int w = 0; w < 2; ++w) {
       mbar_init(&s_full[w], 1);
       mbar_init(&s_empty[w], 128);
@@ -129,21 +137,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int it = 0;
+      int it = 0, kvc = -1, prev_b = -1;  // kvc: kv loads so far - 1
       for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++it) {
         const int s = it % kStages;
         const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) break;
         const int b = tile / p.tiles_per_batch;
         const int r0 = (tile - b * p.tiles_per_batch) * kRows;
+        const bool new_kv = b != prev_b;
+        if (new_kv) {
+          ++kvc;
+          prev_b = b;
+          // the slot's previous batch (two kv loads ago) is no longer read
+          if (kvc >= kKVSlots &&
+              !mbar_wait(&kv_empty[kvc % kKVSlots],
+                         static_cast<uint32_t>((kvc - kKVSlots) / kKVSlots) & 1u, abort_flag,
+                         p.err, DSA_DEVERR_SA_WAIT))
+            break;
+        }
         uint8_t* qs = smem + kOffQ + s * kQBytes;
-        uint8_t* kvs = smem + kOffKV + s * kKVBytes;
-        mbar_arrive_expect_tx(&full[s], p.tx_bytes);
+        mbar_arrive_expect_tx(&full[s], p.tx_bytes + (new_kv ? kKVBytes : 0u));
         tma_load_3d(qs, &tm_q, 0, r0, b, &full[s]);
         tma_load_3d(qs + kQBoxBytes, &tm_q, 64, r0, b, &full[s]);
-        tma_load_3d(kvs, &tm_kv, 0, 0, b, &full[s]);
-        tma_load_3d(kvs + kKVBoxBytes, &tm_kv, 64, 0, b, &full[s]);
         tma_load_3d(smem + kOffIdx + s * kIdxBytes, &tm_idx, 0, r0 / p.heads, b, &full[s]);
+        if (new_kv) {
+          uint8_t* kvs = smem + kOffKV + (kvc % kKVSlots) * kKVBytes;
+          tma_load_3d(kvs, &tm_kv, 0, 0, b, &full[s]);
+          tma_load_3d(kvs + kKVBoxBytes, &tm_kv, 64, 0, b, &full[s]);
+        }
       }
       // Teardown: every load this thread issued must land before the CTA exits.
       for (int i = (it > kStages ? it - kStages : 0); i < it; ++i)
@@ -158,16 +179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kv_base = smem_u32(smem + kOffKV);
       const uint32_t p_base = smem_u32(smem + kOffP);
       bool ok = true;
-      auto issue_mm2 = [&](int i) -> bool {
-        const int s = i % kStages;
+      // kv slot of a tile: the producer's count of batch changes, mod kKVSlots
+      auto issue_mm2 = [&](int i, int slot, bool last_of_batch) -> bool {
         const int w = i & 1;
         const uint32_t jph = static_cast<uint32_t>(i >> 1) & 1u;
         if (!mbar_wait(&p_full[w], jph, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) return false;
         if (!mbar_wait(&o_empty[w], jph ^ 1u, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) return false;
         tc_fence_after();
         const uint32_t d = tmem + 128u + static_cast<uint32_t>(w) * 128u;
-        const uint32_t kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
-        const uint32_t pw = p_base + static_cast<uint32_t>(w) * kPPieces * kPBytes;
+        const uint32_t kvb = kv_base + static_cast<uint32_t>(slot) * kKVBytes;
+        const uint32_t pw = p_base + static_cast<uint32_t>(w) * kPRegion;
 #pragma unroll
         for (int piece = 0; piece < kPPieces; ++piece) {
 #pragma unroll
@@ -183,13 +204,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         umma_commit(&o_full[w]);
+        if (last_of_batch) umma_commit(&kv_empty[slot]);
         return true;
       };
-      int it = 0;
+      int it = 0, kvc = -1, prev_b = -1, prev_slot = 0;
       for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++it) {
         const int s = it % kStages;
         const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
         const int w = it & 1;
+        const int b = tile / p.tiles_per_batch;
+        const bool new_kv = b != prev_b;
+        if (new_kv) {
+          ++kvc;
+          prev_b = b;
+        }
+        const int slot = kvc % kKVSlots;
         const uint32_t jph = static_cast<uint32_t>(it >> 1) & 1u;
         if (!mbar_wait(&full[s], ph, abort_flag, p.err, DSA_DEVERR_SA_WAIT) ||
             !mbar_wait(&s_empty[w], jph ^ 1u, abort_flag, p.err, DSA_DEVERR_SA_WAIT)) {
@@ -199,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(w) * 32u;
         const uint32_t qb = q_base + static_cast<uint32_t>(s) * kQBytes;
-        const uint32_t kvb = kv_base + static_cast<uint32_t>(s) * kKVBytes;
+        const uint32_t kvb = kv_base + static_cast<uint32_t>(slot) * kKVBytes;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
           const uint32_t box = static_cast<uint32_t>(k >> 2);
@@ -210,12 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16(d, ad, bd, idesc1, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[w]);
-        if (it >= 1 && !issue_mm2(it - 1)) {
+        umma_commit(&empty[s]);  // q read: the stage's second arrival
+        if (it >= 1 && !issue_mm2(it - 1, prev_slot, new_kv)) {
           ok = false;
           break;
         }
+        prev_slot = slot;
       }
-      if (ok && it >= 1) issue_mm2(it - 1);
+      if (ok && it >= 1) issue_mm2(it - 1, prev_slot, false);
       // Teardown: all tcgen05 ops issued by this thread complete before exit.
       umma_commit(drain_bar);
       mbar_drain(drain_bar, 0);
@@ -231,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float sink2 = p.sink[h] * kLog2e;
     uint8_t* cnt = smem + kOffCnt + w * 256;
-    const uint32_t p_hi = smem_u32(smem + kOffP + w * kPPieces * kPBytes);
+    uint8_t* preg = smem + kOffP + w * kPRegion;
+    const uint32_t p_hi = smem_u32(preg);
     const uint32_t p_mid = p_hi + kPBytes;
     const uint32_t p_lo = p_mid + kPBytes;
     const uint32_t prow = static_cast<uint32_t>((row >> 3) * 512 + (row & 7) * 16);
@@ -262,7 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < p.topk; ++j) c += (static_cast<long long>(ix[j]) == bin) ? 1 : 0;
         cnt[pr] = static_cast<uint8_t>(c);
       }
+      // the previous output store of this warpgroup has read its staging (the
+      // P region, rewritten below)
+      if (t == 0) bulk_wait_group_read<0>();
       if (!named_bar_and(1 + w, 128, ok)) break;
+      if (t == 0) mbar_arrive(&empty[s]);  // indices counted: the stage's first arrival
 
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&s_full[w], jph, abort_flag, p.err, DSA_DEVERR_SA_WAIT));
       if (ok) {
@@ -321,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&p_full[w]);
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&o_full[w], jph, abort_flag, p.err, DSA_DEVERR_SA_WAIT));
       }
-      uint8_t* ob = smem + kOffQ + s * kQBytes;  // q is dead after mm1: stage out here
+      uint8_t* ob = preg;  // P is dead after mm2: stage the output tile here
       if (ok) {
         tc_fence_after();
         const uint32_t ob_row = smem_u32(ob) + static_cast<uint32_t>(row) * 128u;
@@ -351,8 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_3d(&tm_out, ob, 0, r0, b);
         tma_store_3d(&tm_out, ob + kQBoxBytes, 64, r0, b);
         bulk_commit_group();
-        bulk_wait_group_read<0>();
-        mbar_arrive(&empty[s]);
       }
     }
     if (t == 0) bulk_wait_group<0>();
@@ -430,7 +464,7 @@ int launch(const void* q, const void* kv, const void* idx, const float* sink, vo
   p.topk = topk;
   p.nkv = nkv;
   p.scale_log2 = scale * kLog2e;
-  p.tx_bytes = static_cast<uint32_t>(kQBytes + kKVBytes + tpt * topk * eb);
+  p.tx_bytes = static_cast<uint32_t>(kQBytes + tpt * topk * eb);
   p.sink = sink;
   p.err = err;
 
