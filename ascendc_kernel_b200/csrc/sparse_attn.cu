@@ -290,8 +290,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bin = pr & 31;
         const IdxT* ix = reinterpret_cast<const IdxT*>(smem + kOffIdx + s * kIdxBytes) + ct * p.topk;
         int c = 0;
-        if (bin < p.nkv)
-          for (int j = 0; j < p.topk; ++j) c += (static_cast<long long>(ix[j]) == bin) ? 1 : 0;
+        if (bin < p.nkv) {
+          constexpr int kVec = 16 / static_cast<int>(sizeof(IdxT));  // indices per 16-byte load
+          if (p.topk % kVec == 0) {
+            // 16-byte loads, several in flight (the row is 16-byte aligned)
+#pragma unroll 4
+            for (int j = 0; j < p.topk; j += kVec) {
+              const uint4 v = *reinterpret_cast<const uint4*>(ix + j);
+              if (sizeof(IdxT) == 4) {
+                c += (static_cast<int>(v.x) == bin) + (static_cast<int>(v.y) == bin) +
+                     (static_cast<int>(v.z) == bin) + (static_cast<int>(v.w) == bin);
+              } else {
+                c += (v.x == static_cast<uint32_t>(bin) && v.y == 0u) +
+                     (v.z == static_cast<uint32_t>(bin) && v.w == 0u);
+              }
+            }
+          } else {
+            for (int j = 0; j < p.topk; ++j) c += (static_cast<long long>(ix[j]) == bin) ? 1 : 0;
+          }
+        }
         cnt[pr] = static_cast<uint8_t>(c);
       }
       // the previous output store of this warpgroup has read its staging (the
