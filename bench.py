@@ -349,6 +349,8 @@ def run_ours(args, world, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         time.sleep(0.3)  # let the sampler start before the timed region
+        for _ in range(args.warmup):  # warm again after the idle sleep
+            step()
         torch.cuda.synchronize()
         barrier(world)
         e0.record(stream)
