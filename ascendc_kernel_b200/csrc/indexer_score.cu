@@ -699,10 +699,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tt0 = wg * 8 + tl;
             uint32_t r[32];
             tmem_ld_32x32b_x32(tmem + lane_off + static_cast<uint32_t>(ab * 256 + tt0 * 16), r);
+            // both tokens' interval chains first (one basic block, so their
+            // instructions interleave), then their queue entries and keys
+            uint32_t prs[2][16];
+            uint32_t tlo[2], thi[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               const int tt = tt0 + j;
-              const bool active = k < nvs[tt];
               // Each head score s_h is known to lie in [v - E, v + E] (E = q_h's
               // norm bound times kvn); carry the interval [RNE(v-E), RNE(v+E)]
               // through relu, *w (bf16 RNE, both monotone) and the head sum
@@ -710,7 +713,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               // same bf16, that is the exact score. The ends v +- E come from
               // one directed-rounding fma per two heads.
               float slo[4] = {0.f, 0.f, 0.f, 0.f}, shi[4] = {0.f, 0.f, 0.f, 0.f};
-              uint32_t prs[16];
 #pragma unroll
               for (int h4 = 0; h4 < 4; ++h4) {
                 const float4 qv4 = reinterpret_cast<const float4*>(qn + tt * 16)[h4];
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int i = hp * 2 + m;
                     uint32_t pr;  // upper half RNE(v+E), lower half RNE(v-E)
                     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(hv[m]), "f"(lv[m]));
-                    prs[h + m] = pr;
+                    prs[j][h + m] = pr;
                     uint32_t e2 = __byte_perm(pr, 0, psa[i]);
                     asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
                     asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
@@ -745,10 +747,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float hi_sum = __fadd_ru(__fadd_ru(shi[0], shi[1]), __fadd_ru(shi[2], shi[3]));
               uint32_t tp;
               asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(tp) : "f"(hi_sum), "f"(lo_sum));
-              uint32_t tlo = tp & 0xFFFFu, thi = tp >> 16;
-              if (tlo == 0x8000u) tlo = 0;  // -0 == +0
-              if (thi == 0x8000u) thi = 0;
-              const bool need = active && tlo != thi;
+              tlo[j] = tp & 0xFFFFu;
+              thi[j] = tp >> 16;
+              if (tlo[j] == 0x8000u) tlo[j] = 0;  // -0 == +0
+              if (thi[j] == 0x8000u) thi[j] = 0;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int tt = tt0 + j;
+              const bool active = k < nvs[tt];
+              const bool need = active && tlo[j] != thi[j];
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {
@@ -760,16 +768,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                   e[0] = (static_cast<uint32_t>(s) << 28) | (static_cast<uint32_t>(tt) << 16) |
                          static_cast<uint32_t>(k);
 #pragma unroll
-                  for (int h = 0; h < 16; ++h) e[1 + h] = prs[h];
+                  for (int h = 0; h < 16; ++h) e[1 + h] = prs[j][h];
                   e[17] = __float_as_uint(kvn);
                 }
                 rq_n += __popc(bal);
               }
               if (active && !need) {
                 if (gs) {
-                  gs[tt * p.score_ld + k] = static_cast<uint16_t>(tlo);
+                  gs[tt * p.score_ld + k] = static_cast<uint16_t>(tlo[j]);
                 } else {
-                  const uint32_t ord = (tlo & 0x8000u) ? (~tlo & 0xFFFFu) : (tlo | 0x8000u);
+                  const uint32_t ord = (tlo[j] & 0x8000u) ? (~tlo[j] & 0xFFFFu) : (tlo[j] | 0x8000u);
                   keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
                 }
               }
