@@ -416,7 +416,7 @@ def run_ours(args, world, rank, local):
         e2e_step(i)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_steps = max(3, min(args.steps, 10))
+    e2e_steps = max(3, min(args.steps, 40))
     e0.record(s_in)
     for i in range(e2e_steps):
         e2e_step(i)
