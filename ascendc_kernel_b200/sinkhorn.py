@@ -11,7 +11,15 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from ._native import call
+from ._native import check, lib
+
+_fwd = None  # the bound C entry point, looked up once
+
+try:  # the current stream's raw handle without building a Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    def _raw_stream(device: int) -> int:
+        return torch.cuda.current_stream(device).cuda_stream
 
 
 def sinkhorn(x: torch.Tensor, repeat: int = 10, eps: float = 1e-6,
@@ -19,18 +27,30 @@ def sinkhorn(x: torch.Tensor, repeat: int = 10, eps: float = 1e-6,
     """softmax(-1)+eps, then 2*repeat-1 alternating column/row normalisations.
 
     x [..., 4, 4] fp32 on CUDA. Semantics of reference/task3_v0_ref.py:8-14.
+    The whole call is a few microseconds of GPU work, so the host side is kept
+    short: the entry point is bound once and the device guard is entered only
+    when x lives on a device other than the current one.
     """
+    global _fwd
     assert x.is_cuda and x.dtype == torch.float32, "x must be a CUDA fp32 tensor"
     assert x.shape[-1] == 4 and x.shape[-2] == 4, "kernel specialised to mhc = 4"
     assert repeat >= 1
     x = x.contiguous()
     if out is None:
         out = torch.empty_like(x)
+    if _fwd is None:
+        _fwd = lib().dsa_sinkhorn_fwd
     n_mat = x.numel() // 16
-    stream = torch.cuda.current_stream(x.device).cuda_stream
-    with torch.cuda.device(x.device):
-        call("dsa_sinkhorn_fwd", x.data_ptr(), out.data_ptr(), n_mat, 4, int(repeat),
-             float(eps), stream)
+    dev = x.get_device()
+    if dev == torch.cuda.current_device():
+        st = _fwd(x.data_ptr(), out.data_ptr(), n_mat, 4, int(repeat), float(eps),
+                  _raw_stream(dev))
+    else:
+        with torch.cuda.device(dev):
+            st = _fwd(x.data_ptr(), out.data_ptr(), n_mat, 4, int(repeat), float(eps),
+                      _raw_stream(dev))
+    if st != 0:
+        check("dsa_sinkhorn_fwd", st)
     return out
 
 
