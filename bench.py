@@ -217,7 +217,33 @@ def bench_other_ops(dev):
         sk.sinkhorn(x, 10, 1e-6, out=y)
     e1.record()
     torch.cuda.synchronize()
-    res["sinkhorn"] = {"us_per_call": e0.elapsed_time(e1) * 1e3 / n,
+    us_call = e0.elapsed_time(e1) * 1e3 / n
+
+    # device time per kernel and the latency floor (an empty kernel), both
+    # from CUDA-graph replays of 50 launches, so host overhead drops out
+    def graph_us(fn, reps=50):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    k_us = graph_us(lambda: sk.sinkhorn(x, 10, 1e-6, out=y))
+    floor_us = graph_us(lambda: torch.cuda._sleep(0))
+    res["sinkhorn"] = {"us_per_call": us_call, "kernel_us": k_us,
+                       "launch_floor_us": floor_us, "kernel_over_floor": k_us / floor_us,
                        "shape": "[1,1024,4,4] fp32, repeat 10"}
     try:
         from ascendc_kernel_b200 import indexer as ix
