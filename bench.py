@@ -519,6 +519,18 @@ def run_profile_case(args):
     from ascendc_kernel_b200 import sparse_attn as sa
 
     dev = torch.device("cuda", 0)
+    if args.profile == "sk":
+        # Sinkhorn at the reference shape [1,1024,4,4] (64 KB), W + K calls
+        from ascendc_kernel_b200 import sinkhorn as sk
+
+        torch.manual_seed(0)
+        x = torch.randn(1, 1024, 4, 4, device=dev)
+        y = torch.empty_like(x)
+        for _ in range(args.warmup + args.steps):
+            sk.sinkhorn(x, 10, 1e-6, out=y)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "sk", "launches": args.warmup + args.steps}))
+        return
     if args.profile == "ix":
         from ascendc_kernel_b200 import indexer as ix
 
@@ -572,7 +584,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa", "ix", "chain", "fchain"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix", "chain", "fchain", "sk"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()
