@@ -64,6 +64,7 @@ def make(b, m, h, nkv, topk, dtype=torch.int32, lo=0, seed=0, sink_std=0.0):
     (1, 50, 64, 32, 32, torch.int32),     # topk 32
     (4, 300, 64, 32, 4, torch.int32),     # topk 4
     (1, 700, 64, 8, 16, torch.int64),     # heavy multiplicities
+    (600, 2, 64, 32, 16, torch.int32),    # one tile per batch: a new kv slot every tile
 ])
 def test_shapes(cuda_device, b, m, h, nkv, topk, dtype):
     q, kv, idx, sink = make(b, m, h, nkv, topk, dtype, seed=b * 1000 + m, sink_std=1.0)
