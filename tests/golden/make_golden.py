@@ -252,9 +252,12 @@ def make_indexer_full(ref: str) -> tuple[dict, dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("DSA_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("DSA_REFERENCE_DIR"),
+                    help="checkout of the reference repository (or set DSA_REFERENCE_DIR)")
     ap.add_argument("--skip-full", action="store_true")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref or DSA_REFERENCE_DIR: the reference checkout to import")
     torch.set_num_threads(os.cpu_count() or 1)
     np.savez_compressed(os.path.join(HERE, "sinkhorn.npz"), **make_sinkhorn(a.ref))
     np.savez_compressed(os.path.join(HERE, "sparse_attn.npz"), **make_sparse_attn(a.ref))
