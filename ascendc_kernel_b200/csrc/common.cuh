@@ -488,6 +488,22 @@ __device__ __forceinline__ float add_ru_bf16lo(uint32_t w, float acc) {
       : "=f"(d) : "r"(w), "f"(acc));
   return d;
 }
+// a.lo * b.lo + c (a.hi * b.hi + c) for the bf16 halves of a and b, one
+// rounding to nearest, no separate conversions.
+__device__ __forceinline__ float fma_bf16lo(uint32_t a, uint32_t b, float c) {
+  float d;
+  asm("{.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %3;}"
+      : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_bf16hi(uint32_t a, uint32_t b, float c) {
+  float d;
+  asm("{.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, ah, bh, %3;}"
+      : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
 // Products of the low (high) bf16 halves of a and b: exact in fp32 up to
 // underflow (8 x 8 significand bits), without separate conversions.
 __device__ __forceinline__ float mul_bf16lo(uint32_t a, uint32_t b) {

@@ -93,20 +93,22 @@ __device__ __forceinline__ int64_t n_valid(const Params& p, int64_t t) {
 }
 
 // Row norm (upper bound) of a 64-wide bf16 row stored SW128 in smem.
+// The squares go straight from the bf16 halves into four partial sums (mixed
+// bf16 x bf16 + fp32 fma, one rounding each); norm_upper's bound holds for any
+// summation order of the 64 terms.
 __device__ __forceinline__ float row_norm64(const uint8_t* base, int row) {
-  float ss = 0.f;
+  float ss[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int ch = 0; ch < 8; ++ch) {
     const uint4 v = *reinterpret_cast<const uint4*>(base + sw128_off(row, ch));
     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float lo = bf16lo_to_f32(w4[e]), hi = bf16hi_to_f32(w4[e]);
-      ss = fmaf(lo, lo, ss);
-      ss = fmaf(hi, hi, ss);
+      ss[e] = fma_bf16lo(w4[e], w4[e], ss[e]);
+      ss[e] = fma_bf16hi(w4[e], w4[e], ss[e]);
     }
   }
-  return norm_upper(ss, kDim);
+  return norm_upper((ss[0] + ss[1]) + (ss[2] + ss[3]), kDim);
 }
 
 // score key of candidate k from its 16 correctly rounded bf16 head scores:
