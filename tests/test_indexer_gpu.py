@@ -151,6 +151,7 @@ def _random_case(batch, seqlen, start_pos, offset, ratio, topk, dim=256, qlora=1
     (2, 40, 24, 3, 4, 8),       # decode: no causal mask, + offset
     (1, 1, 99, 0, 4, 16),       # single-token decode
     (2, 600, 0, 0, 1, 256),     # 600 candidates, top-256
+    (1, 1024, 0, 0, 1, 256),    # the fused path's limits: 1024 candidates, top-256
 ])
 def test_forward_shapes_equal_oracle(cuda_device, batch, seqlen, start_pos, offset, ratio, topk):
     got, want = _random_case(batch, seqlen, start_pos, offset, ratio, topk,
