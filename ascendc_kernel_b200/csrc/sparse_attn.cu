@@ -345,11 +345,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 32; ++k) {
           const uint32_t c = (cw[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
           const float z = __uint_as_float(sv[k]) * p.scale_log2;
-          e[k] = c != 0u ? static_cast<float>(c) * exp2f(z - mx) : 0.f;
+          e[k] = c != 0u ? static_cast<float>(c) * ex2_approx(z - mx) : 0.f;
           sum += e[k];
         }
-        sum += exp2f(sink2 - mx);
-        const float inv = 1.0f / sum;
+        sum += ex2_approx(sink2 - mx);
+        const float inv = __frcp_rn(sum);  // the same value as 1 / sum, fewer steps
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           // p = hi + mid + lo exactly up to the last 8 bits of lo: each
