@@ -352,19 +352,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = __frcp_rn(sum);  // the same value as 1 / sum, fewer steps
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          // p = hi + mid + lo exactly up to the last 8 bits of lo: each
-          // residual (p - hi, r1 - mid) is exact in fp32.
+          // p = hi + mid + lo exactly up to the rounding of lo: hi and mid are
+          // truncations to bf16 (byte permutes) and each residual (p - hi,
+          // r - mid) is exact in fp32; two weights per f32x2 instruction.
           uint32_t hi[4], mid[4], lo[4];
+          const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float a0 = e[c * 8 + 2 * j] * inv;
-            const float a1 = e[c * 8 + 2 * j + 1] * inv;
-            hi[j] = pack_bf16x2(a0, a1);
-            const float r0 = a0 - bf16_bits_to_float(hi[j] & 0xFFFFu);
-            const float r1 = a1 - bf16_bits_to_float(hi[j] >> 16);
-            mid[j] = pack_bf16x2(r0, r1);
-            lo[j] = pack_bf16x2(r0 - bf16_bits_to_float(mid[j] & 0xFFFFu),
-                                r1 - bf16_bits_to_float(mid[j] >> 16));
+            float a0, a1;
+            f2_unpack(f2_mul(f2_pack(e[c * 8 + 2 * j], e[c * 8 + 2 * j + 1]), inv2), a0, a1);
+            // hi and mid by truncation (byte permutes), lo rounded
+            hi[j] = __byte_perm(__float_as_uint(a0), __float_as_uint(a1), 0x7632u);
+            float r0, r1;
+            f2_unpack(f2_sub(f2_pack(a0, a1),
+                             f2_pack(__uint_as_float(__float_as_uint(a0) & 0xFFFF0000u),
+                                     __uint_as_float(__float_as_uint(a1) & 0xFFFF0000u))),
+                      r0, r1);
+            mid[j] = __byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632u);
+            float q0, q1;
+            f2_unpack(f2_sub(f2_pack(r0, r1),
+                             f2_pack(__uint_as_float(__float_as_uint(r0) & 0xFFFF0000u),
+                                     __uint_as_float(__float_as_uint(r1) & 0xFFFF0000u))),
+                      q0, q1);
+            lo[j] = pack_bf16x2(q0, q1);
           }
           st_shared_v4(p_hi + prow + c * 128, hi[0], hi[1], hi[2], hi[3]);
           st_shared_v4(p_mid + prow + c * 128, mid[0], mid[1], mid[2], mid[3]);
