@@ -332,22 +332,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           cw[0] = c0.x; cw[1] = c0.y; cw[2] = c0.z; cw[3] = c0.w;
           cw[4] = c1.x; cw[5] = c1.y; cw[6] = c1.z; cw[7] = c1.w;
         }
-        float mx = sink2;
+        // logits of the selected rows (-inf for rows of count 0), their max as a
+        // tree, and the multiplicities as floats from their bits (c < 2^8: the
+        // low bits of 2^23 + c), so that no conversion instruction is needed
+        float z[32], cf[32];
+        const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const uint32_t c = (cw[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
-          const float z = __uint_as_float(sv[k]) * p.scale_log2;
-          if (c != 0u) mx = fmaxf(mx, z);
+        for (int k = 0; k < 32; k += 2) {
+          float z0, z1;
+          f2_unpack(f2_mul(f2_pack(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1])), sc2), z0,
+                    z1);
+          const uint32_t c0 = (cw[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
+          const uint32_t c1 = (cw[k >> 2] >> (((k + 1) & 3) * 8)) & 0xFFu;
+          z[k] = c0 != 0u ? z0 : -INFINITY;
+          z[k + 1] = c1 != 0u ? z1 : -INFINITY;
+          cf[k] = __uint_as_float(0x4B000000u | c0) - 8388608.0f;
+          cf[k + 1] = __uint_as_float(0x4B000000u | c1) - 8388608.0f;
         }
+        float m8[11];
+#pragma unroll
+        for (int i = 0; i < 10; ++i) m8[i] = fmax3(z[3 * i], z[3 * i + 1], z[3 * i + 2]);
+        m8[10] = fmax3(z[30], z[31], sink2);
+        const float mx = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                                     fmax3(m8[6], m8[7], m8[8])),
+                               fmaxf(m8[9], m8[10]));
         float e[32];
-        float sum = 0.f;
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int k = 0; k < 32; ++k) {
-          const uint32_t c = (cw[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
-          const float z = __uint_as_float(sv[k]) * p.scale_log2;
-          e[k] = c != 0u ? static_cast<float>(c) * ex2_approx(z - mx) : 0.f;
-          sum += e[k];
+          e[k] = cf[k] * ex2_approx(z[k] - mx);  // 2^-inf = 0 for unselected rows
+          ps[k & 3] += e[k];
         }
+        float sum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         sum += ex2_approx(sink2 - mx);
         const float inv = __frcp_rn(sum);  // the same value as 1 / sum, fewer steps
 #pragma unroll
