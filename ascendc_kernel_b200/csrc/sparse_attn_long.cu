@@ -390,16 +390,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           z[2 * q4 + 1] = f2_fma(f2_pack(__uint_as_float(v[o + 2]), __uint_as_float(v[o + 3])),
                                  scale2, f2_pack(bv.z, bv.w));
         }
-        float m0 = -INFINITY, m1 = -INFINITY;
+        // the max as a tree of three-input maxes (64 values, depth 4)
+        float t1[22];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float a0, a1, b0, b1;
-          f2_unpack(z[i], a0, a1);
-          f2_unpack(z[i + 1], b0, b1);
-          m0 = fmax3(m0, a0, a1);
-          m1 = fmax3(m1, b0, b1);
+        for (int i = 0; i < 21; ++i) {
+          float a0, a1, b0, b1, c0, c1;
+          const int e0 = 3 * i, e1 = 3 * i + 1, e2 = 3 * i + 2;  // elements of the 64
+          f2_unpack(z[e0 >> 1], a0, a1);
+          f2_unpack(z[e1 >> 1], b0, b1);
+          f2_unpack(z[e2 >> 1], c0, c1);
+          t1[i] = fmax3((e0 & 1) ? a1 : a0, (e1 & 1) ? b1 : b0, (e2 & 1) ? c1 : c0);
         }
-        mh = fmaxf(m0, m1);
+        {
+          float a0, a1;
+          f2_unpack(z[31], a0, a1);
+          t1[21] = a1;  // element 63
+        }
+        float t2[8];
+#pragma unroll
+        for (int i = 0; i < 7; ++i) t2[i] = fmax3(t1[3 * i], t1[3 * i + 1], t1[3 * i + 2]);
+        t2[7] = t1[21];
+        mh = fmaxf(fmax3(t2[0], t2[1], t2[2]), fmax3(t2[3], t2[4], fmax3(t2[5], t2[6], t2[7])));
       }
       // the item's first chunk always agrees a reference; later chunks only when
       // some row of the quarter went more than 2^kRescaleLog2 above its reference
