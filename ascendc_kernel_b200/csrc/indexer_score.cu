@@ -256,8 +256,9 @@ __device__ __forceinline__ uint32_t drained_key(const uint32_t* e, const uint32_
 
 // Per-warp queue of (token, candidate) pairs of the last one or two chunks
 // whose score could not be certified. Entry: word 0 = kv stage << 28 | token
-// slot << 16 | candidate k, words 1..16 = per head the bf16 pair {RNE(v+E),
-// RNE(v-E)} of the interval that holds the head's exact bf16 score, word 17 =
+// slot << 16 | candidate k, words 1..16 = per head the bf16 pair
+// {relu(RNE(v+E)), relu(RNE(v-E))} of the interval that holds the head's exact
+// bf16 score after the relu (a negative score is 0 either way), word 17 =
 // the kv row's norm bound times kGamma (19 words: an odd stride keeps the
 // lanes' reads of one word on distinct banks).
 constexpr int kRqWords = 19;
@@ -734,11 +735,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                   for (int m = 0; m < 2; ++m) {
                     const int i = hp * 2 + m;
-                    uint32_t pr;  // upper half RNE(v+E), lower half RNE(v-E)
-                    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(hv[m]), "f"(lv[m]));
+                    // upper half relu(RNE(v+E)), lower half relu(RNE(v-E)): the
+                    // relu rides on the conversion (RNE is monotone and keeps signs)
+                    uint32_t pr;
+                    asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(hv[m]), "f"(lv[m]));
                     prs[j][h + m] = pr;
                     uint32_t e2 = __byte_perm(pr, 0, psa[i]);
-                    asm("max.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(0u));
                     asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(e2) : "r"(e2), "r"(wpa[i]));
                     slo[i] = add_rd_bf16lo(e2, slo[i]);
                     shi[i] = add_ru_bf16hi(e2, shi[i]);
