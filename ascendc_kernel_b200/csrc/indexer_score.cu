@@ -760,7 +760,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 2; ++j) {
               const int tt = tt0 + j;
               const bool active = k < nvs[tt];
-              const bool need = active && tlo[j] != thi[j];
+              // a NaN head score (relu keeps it NaN here) goes the exact way, where
+              // the relu maps it to 0 like the oracle's
+              const bool need = active && (tlo[j] != thi[j] || (tlo[j] & 0x7FFFu) > 0x7F80u);
               const uint32_t bal = __ballot_sync(0xFFFFFFFFu, need);
               if (bal) {
                 if (rq_n + __popc(bal) > kRqCap) {

@@ -202,6 +202,23 @@ def test_long_candidate_lists(cuda_device, batch, seqlen, n_cand, topk, start_po
     assert _native.device_error(cuda_device.index) == 0
 
 
+def test_score_nonfinite_inputs(cuda_device):
+    """Inf and NaN in q: a NaN head score is relu'd to 0, as the oracle does."""
+    batch, seqlen, n_cand, topk = 1, 64, 256, 32
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(batch * seqlen, 16 * 64, generator=g).to(torch.bfloat16)
+    q[3, 5] = float("nan")            # NaN in one head of token 3
+    q[10, 64 * 2 + 7] = float("inf")  # +inf in one head of token 10
+    q[11, 64 * 9 + 1] = float("-inf")
+    w = (torch.randn(batch * seqlen, 16, generator=g) * 0.25).to(torch.bfloat16)
+    kv = torch.randn(batch, n_cand, 64, generator=g).to(torch.bfloat16)
+    got = ix.score_topk(q.to(cuda_device), w.to(cuda_device), kv.to(cuda_device), batch, seqlen,
+                        n_cand, topk, 0, 4, 0).cpu().reshape(batch * seqlen, topk)
+    want, _ = oracle.index_topk(to_u16(q), to_u16(w), to_u16(kv), batch, seqlen, 16, 64, n_cand,
+                                topk, 0, 4, 0)
+    assert torch.equal(got, torch.from_numpy(want))
+
+
 def test_long_candidate_lists_ties(cuda_device):
     got, want = _score_case(1, 60, 2000, 1500, 2000 * 4 - 60, 0, seed=5, dev=cuda_device,
                             ties=True)
