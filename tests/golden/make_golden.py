@@ -21,8 +21,8 @@ Outputs
                       masked bf16 scores) and the reference's top-k indices.
   indexer_full_pin.json / indexer_full_rows.npz
                       full BASELINE shape [8,2600]: the reference's per-row
-                      top-k value lists (as digests) and the comparison of the
-                      oracle against the reference at that size.
+                      top-k index lists and value lists (as digests) and the
+                      comparison of the oracle against the reference at that size.
 """
 
 from __future__ import annotations
@@ -157,10 +157,10 @@ def make_indexer(ref: str) -> dict:
     return out
 
 
-def _row_digest(values_u16: np.ndarray) -> np.ndarray:
-    """8-byte digest of each row of a [rows, K] uint16 array."""
-    out = np.empty(values_u16.shape[0], dtype=np.uint64)
-    for i, row in enumerate(values_u16):
+def _row_digest(values: np.ndarray) -> np.ndarray:
+    """8-byte digest of each row of a [rows, K] array (its raw bytes)."""
+    out = np.empty(values.shape[0], dtype=np.uint64)
+    for i, row in enumerate(values):
         out[i] = np.frombuffer(hashlib.blake2b(row.tobytes(), digest_size=8).digest(),
                                dtype=np.uint64)[0]
     return out
@@ -245,6 +245,7 @@ def make_indexer_full(ref: str) -> tuple[dict, dict]:
     }
     arrays = {
         "ref_value_digest": _row_digest(ref_vals),
+        "ref_index_digest": _row_digest(ref_idx),
         "rows_with_score_mismatch": rows_with_score_diff.astype(np.int64),
     }
     return stats, arrays
