@@ -65,3 +65,58 @@ def test_chain_long_context_shape(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     assert _native.device_error(cuda_device.index) == 0
+
+
+def _oracle_chain(ixm, sam, x, qr, start_pos, offset, q, kv, rows):
+    """sparse_attn_ref(q, kv, sink, Model.forward(x, qr, start_pos, offset)) on the CPU
+    oracle (reference/task2_v0_ref.py:123-144 feeding reference/task1_v0_ref.py:5-24),
+    the attention evaluated on the token positions `rows` only."""
+    import numpy as np
+
+    import oracle
+    from tests.helpers import to_u16
+
+    b, s = x.shape[:2]
+    fc = torch.view_as_real(ixm.freqs_cis[start_pos:start_pos + s].cpu())
+    idx = oracle.indexer_fwd(
+        to_u16(x), to_u16(qr), to_u16(ixm.wq_b.weight), to_u16(ixm.weights_proj.weight),
+        fc[..., 0].contiguous().numpy(), fc[..., 1].contiguous().numpy(), to_u16(ixm.kv_cache),
+        n_heads=16, head_dim=64, rope_dim=32, index_topk=ixm.index_topk, start_pos=start_pos,
+        ratio=ixm.compress_ratio, offset=offset,
+        w_scale=ixm.softmax_scale * ixm.n_heads ** -0.5)
+    qs = np.ascontiguousarray(to_u16(q)[:, rows])
+    ids = np.ascontiguousarray(idx[:, rows])
+    return oracle.sparse_attn(qs, to_u16(kv), ids, sam.attn_sink.detach().cpu().numpy(),
+                              sam.softmax_scale)
+
+
+@pytest.mark.parametrize("b,s,t_cache,topk,n_pool,heads,start_pos,offset,ties,n_rows", [
+    # causal, 2048 candidates at the last token, top-512, integer kv_cache: ties
+    (1, 8192, 2048, 512, 2048, 64, 0, 0, 1, 192),
+    # decode: 2048 candidates for every token, top-1024, index offset into the pool
+    (2, 32, 2048, 1024, 2304, 64, 8160, 256, 2, 32),
+    # the chained configuration's selection: 4096 candidates, top-2048, 128 heads
+    (1, 16, 4096, 2048, 4096, 128, 16368, 0, None, 16),
+])
+def test_chain_matches_oracle(cuda_device, b, s, t_cache, topk, n_pool, heads, start_pos,
+                              offset, ties, n_rows):
+    """The fused call against the oracle's indexer -> attention sequence (the
+    bitmap hand-off is the part only the fused path has)."""
+    import numpy as np
+
+    from tests.helpers import bf16_compare, to_u16
+
+    ixm, sam, x, qr, q, kv = make_case(cuda_device, b, s, t_cache, topk, n_pool, heads,
+                                       start_pos=start_pos, seed=11, tie_levels=ties)
+    got = chain.indexer_sparse_attn(ixm, sam, x, qr, start_pos, offset, q, kv)
+    torch.cuda.synchronize()
+    assert _native.device_error(cuda_device.index) == 0
+    # rows: the last tokens (most candidates) and an even spread over the rest
+    rows = np.unique(np.concatenate([np.linspace(0, s - 1, n_rows // 2).astype(np.int64),
+                                     np.arange(max(0, s - n_rows // 2), s)]))
+    want = _oracle_chain(ixm, sam, x.cpu(), qr.cpu(), start_pos, offset, q.cpu(), kv.cpu(), rows)
+    r = bf16_compare(np.ascontiguousarray(to_u16(got)[:, rows]), want, 1e-2, 1e-2)
+    # long-pool attention tolerance (two-piece bf16 P): see test_sparse_attn_gpu.py
+    assert r["allclose"], r
+    assert r["bit_mismatch"] <= max(4, r["n"] * 1e-2), r
+    assert r["max_abs"] <= 4e-3, r
