@@ -1,35 +1,125 @@
 // Status strings, the per-device error word, device-info cache and the TMA
 // tensor-map encoder used by all entry points.
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "host_util.h"
 
 namespace dsa {
 
-// Per-device error word. Kernels receive its device address (see
-// device_error_word) and OR DSA_DEVERR_* codes into it.
+// Error word of each context that loads this module. Kernels receive its
+// device address (see device_error_word) and OR DSA_DEVERR_* codes into it.
 __device__ unsigned int g_dsa_device_error = 0;
 
-int device_error_word(unsigned int** ptr) {
-  static std::mutex mu;
-  static unsigned int* cache[64] = {nullptr};
-  int dev = 0;
-  int st = cuda_status(cudaGetDevice(&dev));
-  if (st != DSA_OK) return st;
-  if (dev < 0 || dev >= 64) return DSA_ERR_NO_DEVICE;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cache[dev] == nullptr) {
+static thread_local int t_last_cuda_error = 0;
+
+namespace {
+
+typedef CUresult (*PFN_CtxGetCurrent)(CUcontext*);
+typedef CUresult (*PFN_CtxGetId)(CUcontext, unsigned long long*);
+
+struct CtxFns {
+  PFN_CtxGetCurrent get_current = nullptr;
+  PFN_CtxGetId get_id = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+  static CtxFns f;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    st = cuda_status(cudaGetSymbolAddress(&p, g_dsa_device_error));
-    if (st != DSA_OK) return st;
-    cache[dev] = static_cast<unsigned int*>(p);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.get_current = reinterpret_cast<PFN_CtxGetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.get_id = reinterpret_cast<PFN_CtxGetId>(p);
+  });
+  return f;
+}
+
+// (context id, key, tag) -> value; a handful of entries per context. The key
+// is a symbol (tag -1) or a kernel (tag = the attribute set on it).
+struct CtxEntry {
+  unsigned long long ctx;
+  const void* key;
+  int tag;
+  void* value;
+};
+std::mutex g_ctx_mu;
+std::vector<CtxEntry> g_ctx_cache;
+
+bool ctx_lookup(unsigned long long ctx, const void* key, int tag, void** value) {
+  std::lock_guard<std::mutex> lock(g_ctx_mu);
+  for (const CtxEntry& e : g_ctx_cache)
+    if (e.ctx == ctx && e.key == key && e.tag == tag) {
+      *value = e.value;
+      return true;
+    }
+  return false;
+}
+
+void ctx_store(unsigned long long ctx, const void* key, int tag, void* value) {
+  std::lock_guard<std::mutex> lock(g_ctx_mu);
+  for (const CtxEntry& e : g_ctx_cache)
+    if (e.ctx == ctx && e.key == key && e.tag == tag) return;
+  g_ctx_cache.push_back(CtxEntry{ctx, key, tag, value});
+}
+
+}  // namespace
+
+int current_context_id(unsigned long long* id) {
+  *id = 0;
+  const CtxFns& f = ctx_fns();
+  if (f.get_current == nullptr || f.get_id == nullptr) return DSA_ERR_CUDA;
+  CUcontext c = nullptr;
+  CUresult r = f.get_current(&c);
+  if (r == CUDA_SUCCESS && c != nullptr) r = f.get_id(c, id);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return DSA_ERR_CUDA;
   }
-  *ptr = cache[dev];
   return DSA_OK;
 }
 
-static thread_local int t_last_cuda_error = 0;
+int context_symbol_address(const void* symbol, void** out) {
+  unsigned long long id = 0;
+  int st = current_context_id(&id);
+  if (st != DSA_OK) return st;
+  if (id != 0 && ctx_lookup(id, symbol, -1, out)) return DSA_OK;
+  void* p = nullptr;
+  st = cuda_status(cudaGetSymbolAddress(&p, symbol));
+  if (st != DSA_OK) return st;
+  // with no context current before, the lookup has made the device's primary one current
+  if (id == 0 && (st = current_context_id(&id)) != DSA_OK) return st;
+  if (id != 0) ctx_store(id, symbol, -1, p);
+  *out = p;
+  return DSA_OK;
+}
+
+int set_func_attribute_once(const void* func, cudaFuncAttribute attr, int value) {
+  unsigned long long id = 0;
+  int st = current_context_id(&id);
+  if (st != DSA_OK) return st;
+  void* seen = nullptr;
+  const int tag = static_cast<int>(attr);
+  if (id != 0 && ctx_lookup(id, func, tag, &seen)) return DSA_OK;
+  st = cuda_status(cudaFuncSetAttribute(func, attr, value));
+  if (st != DSA_OK) return st;
+  if (id == 0 && (st = current_context_id(&id)) != DSA_OK) return st;
+  if (id != 0) ctx_store(id, func, tag, const_cast<void*>(func));
+  return DSA_OK;
+}
+
+int device_error_word(unsigned int** ptr) {
+  void* p = nullptr;
+  const int st = context_symbol_address(&g_dsa_device_error, &p);
+  if (st == DSA_OK) *ptr = static_cast<unsigned int*>(p);
+  return st;
+}
 
 int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return DSA_OK;
@@ -133,8 +223,8 @@ int dsa_device_error_read(int device, unsigned int* code_out, int clear) {
   int prev = 0;
   int st = dsa::cuda_status(cudaGetDevice(&prev));
   if (st != DSA_OK) return st;
-  st = dsa::cuda_status(cudaSetDevice(device));
-  if (st != DSA_OK) return st;
+  // the current context stays (it may be one the caller created) when it is on `device`
+  if (device != prev && (st = dsa::cuda_status(cudaSetDevice(device))) != DSA_OK) return st;
   st = dsa::cuda_status(cudaDeviceSynchronize());
   if (st == DSA_OK) {
     unsigned int v = 0;
@@ -147,7 +237,7 @@ int dsa_device_error_read(int device, unsigned int* code_out, int clear) {
       }
     }
   }
-  cudaSetDevice(prev);
+  if (device != prev) cudaSetDevice(prev);
   return st;
 }
 

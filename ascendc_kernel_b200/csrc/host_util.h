@@ -31,8 +31,24 @@ int encode_tensor_map(CUtensorMap* tm, CUtensorMapDataType dtype, int rank, cons
                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                       CUtensorMapSwizzle swizzle);
 
-// Device address of the per-device error word of the current device.
+// Device address of the error word in the calling thread's current context.
 int device_error_word(unsigned int** ptr);
+
+// Id of the calling thread's current CUDA context (cuCtxGetId), 0 when no
+// context is current yet. A module-scope __device__ variable has its own
+// address in every context, and a kernel attribute is set per context, so the
+// caches below are keyed by this id, not by the device ordinal.
+int current_context_id(unsigned long long* id);
+
+// Device address of the module-scope __device__ variable whose host-side
+// stand-in is `symbol`, in the current context (looked up once per context).
+int context_symbol_address(const void* symbol, void** out);
+
+// cudaFuncSetAttribute(func, attr, value), once per context, kernel and attribute.
+int set_func_attribute_once(const void* func, cudaFuncAttribute attr, int value);
+inline int set_max_dynamic_smem(const void* func, int bytes) {
+  return set_func_attribute_once(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -8,14 +8,13 @@
 // library, of kNoAllocScratchBytes per device; every device that loads the
 // library keeps it until the process exits.
 //
-// The first call on a device looks up the device address of that array
-// (cudaGetSymbolAddress) and caches it; make that first call before any
-// stream capture. All calls on a device share the array, so calls whose
+// The first call in a CUDA context (the device's primary context, or one the
+// caller created and made current) looks up the device address of that array
+// (cudaGetSymbolAddress) and caches it for that context; make that first call
+// before any stream capture. All calls on a device share the array, so calls whose
 // kernels overlap on the GPU (e.g. on two streams) race on it; every byte a
 // call reads from the array is written earlier by the same call, so nothing
 // has to be cleared between calls.
-#include <mutex>
-
 #include "common.cuh"
 #include "host_util.h"
 
@@ -26,23 +25,11 @@ constexpr size_t kNoAllocScratchBytes = size_t{128} << 20;  // 128 MiB
 
 static __device__ __align__(256) unsigned char g_indexer_scratch[kNoAllocScratchBytes];
 
-int scratch_address(void** out) {
-  static std::mutex mu;
-  static void* cache[64] = {nullptr};
-  int dev = 0;
-  int st = cuda_status(cudaGetDevice(&dev));
-  if (st != DSA_OK) return st;
-  if (dev < 0 || dev >= 64) return DSA_ERR_NO_DEVICE;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cache[dev] == nullptr) {
-    void* p = nullptr;
-    st = cuda_status(cudaGetSymbolAddress(&p, g_indexer_scratch));
-    if (st != DSA_OK) return st;
-    cache[dev] = p;
-  }
-  *out = cache[dev];
-  return DSA_OK;
-}
+// The array's device address in the calling thread's current context: looked
+// up with cudaGetSymbolAddress the first time a context calls, then cached
+// under the context's id (each context that loads the library has its own copy
+// of the array at its own address).
+int scratch_address(void** out) { return context_symbol_address(g_indexer_scratch, out); }
 
 }  // namespace
 }  // namespace dsa

@@ -649,14 +649,6 @@ __global__ void __launch_bounds__(kFixWarps * 32)
   }
 }
 
-int set_smem_attr(const void* fn, int bytes, bool* done, int dev) {
-  if (done[dev]) return DSA_OK;
-  const int st = cuda_status(
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  if (st == DSA_OK) done[dev] = true;
-  return st;
-}
-
 }  // namespace ixp
 
 int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
@@ -721,9 +713,7 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
   p.b_n3 = b_n3;
   p.open_bits = open_bits;
   p.err = err;
-  static bool attr_done[64] = {false};
-  st = set_smem_attr(reinterpret_cast<const void*>(qproj_rope_kernel), kQSmem, attr_done,
-                     di.device);
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(qproj_rope_kernel), kQSmem);
   if (st != DSA_OK) return st;
   const int grid = p.units < di.num_sms ? p.units : di.num_sms;
   qproj_rope_kernel<<<grid, kQThreads, kQSmem, stream>>>(tm_a, tm_b, tm_q, p);
@@ -743,15 +733,11 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
   f.sin_tab = sin_tab;
   f.open_bits = open_bits;
   f.q = static_cast<uint16_t*>(q_out);
-  static bool fix_attr_done[64] = {false};
-  if (!fix_attr_done[di.device]) {
-    // shared memory first: the launch relies on 8 resident blocks per SM
-    st = cuda_status(cudaFuncSetAttribute(reinterpret_cast<const void*>(qproj_fixup_kernel),
-                                          cudaFuncAttributePreferredSharedMemoryCarveout,
-                                          cudaSharedmemCarveoutMaxShared));
-    if (st != DSA_OK) return st;
-    fix_attr_done[di.device] = true;
-  }
+  // shared memory first: the launch relies on 8 resident blocks per SM
+  st = set_func_attribute_once(reinterpret_cast<const void*>(qproj_fixup_kernel),
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+  if (st != DSA_OK) return st;
   const int64_t fblocks = (rows + kFixWarps - 1) / kFixWarps;
   const int64_t fgrid = fblocks < 8 * di.num_sms ? fblocks : 8 * di.num_sms;
   qproj_fixup_kernel<<<static_cast<unsigned>(fgrid), kFixWarps * 32, 0, stream>>>(f);

@@ -890,13 +890,8 @@ int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_b
   p.scores = static_cast<uint16_t*>(scores);
   p.score_ld = n_cand;
   p.err = err;
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    st = cuda_status(cudaFuncSetAttribute(score_topk_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(score_topk_kernel), kSmem);
+  if (st != DSA_OK) return st;
   const int grid = p.units < di.num_sms ? p.units : di.num_sms;
   score_topk_kernel<<<grid, kThreads, kSmem, stream>>>(tm_q, tm_kv, p);
   return cuda_status(cudaGetLastError());

@@ -163,13 +163,8 @@ __global__ void __launch_bounds__(kThreads)
 template <int J>
 int launch_sort(const Params& p, const DeviceInfo& di, cudaStream_t stream) {
   const int smem = (kWarps * 256 + 32 + 2 * kThreads * J) * 4;
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    const int st = cuda_status(cudaFuncSetAttribute(
-        topk_sort_kernel<J>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
+  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(topk_sort_kernel<J>), smem);
+  if (st != DSA_OK) return st;
   int64_t grid = static_cast<int64_t>(di.num_sms) * 4;
   if (grid > p.rows) grid = p.rows;
   topk_sort_kernel<J><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);

@@ -469,13 +469,8 @@ int launch_wproj_s8(const void* x, const void* wp, void* w_out, int64_t rows, in
   p.wp = static_cast<const uint16_t*>(wp);
   p.w_out = static_cast<uint16_t*>(w_out);
   p.err = err;
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    st = cuda_status(cudaFuncSetAttribute(wproj_s8_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(wproj_s8_kernel), kSmem);
+  if (st != DSA_OK) return st;
   const int grid = p.m_tiles < di.num_sms ? p.m_tiles : di.num_sms;
   wproj_s8_kernel<<<grid, kThreads, kSmem, stream>>>(tm_a, tm_b, p);
   return cuda_status(cudaGetLastError());

@@ -511,13 +511,8 @@ int launch(const void* q, const void* kv, const void* idx, const float* sink, vo
   p.sink = sink;
   p.err = err;
 
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    st = cuda_status(cudaFuncSetAttribute(sa_fwd_kernel<IdxT>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(sa_fwd_kernel<IdxT>), kSmemBytes);
+  if (st != DSA_OK) return st;
   const int grid = static_cast<int>(total < di.num_sms ? total : di.num_sms);
   sa_fwd_kernel<IdxT><<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_kv, tm_idx, tm_out, p);
   return cuda_status(cudaGetLastError());

@@ -743,17 +743,10 @@ int launch(const void* q, const void* kv, const void* idx, const uint32_t* mask,
   p.mask_words = mask_words;
   p.mask_offset = mask_offset;
   p.err = err;
-  static bool attr_done[64] = {false};
-  if (!attr_done[di.device]) {
-    st = cuda_status(cudaFuncSetAttribute(sa_long_kernel<int32_t>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    if (st == DSA_OK)
-      st = cuda_status(cudaFuncSetAttribute(sa_long_kernel<int64_t>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kSmemBytes));
-    if (st != DSA_OK) return st;
-    attr_done[di.device] = true;
-  }
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(sa_long_kernel<int32_t>), kSmemBytes);
+  if (st == DSA_OK)
+    st = set_max_dynamic_smem(reinterpret_cast<const void*>(sa_long_kernel<int64_t>), kSmemBytes);
+  if (st != DSA_OK) return st;
   const int64_t grid64 = p.total_items < di.num_sms ? p.total_items : di.num_sms;
   sa_long_kernel<IdxT><<<static_cast<unsigned>(grid64), kThreads, kSmemBytes, stream>>>(
       tm_q, tm_kv, tm_out, p);

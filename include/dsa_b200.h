@@ -53,7 +53,10 @@ const char* dsa_status_string(int status);
 int dsa_last_cuda_error(void);
 
 /* Synchronizes `device`, then stores the device error word in *code_out and,
- * when `clear` is non-zero, resets it to 0. Returns DSA_OK or DSA_ERR_CUDA. */
+ * when `clear` is non-zero, resets it to 0. The word belongs to a CUDA context:
+ * the calling thread's current one when it is on `device` (the primary context,
+ * or one the caller created), else the primary context of `device`.
+ * Returns DSA_OK or DSA_ERR_CUDA. */
 int dsa_device_error_read(int device, unsigned int* code_out, int clear);
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
@@ -188,8 +191,10 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
  * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
  * <= 128 MiB, i.e. at most 25,981 tokens (batch*seqlen) at 16 heads x 64 dims
  * with n_cand <= 1024 and topk <= 256 (fewer with a score buffer); larger
- * requests return DSA_ERR_WORKSPACE and launch nothing. The first call on a
- * device looks up the array's address; make it before any stream capture.
+ * requests return DSA_ERR_WORKSPACE and launch nothing. Each CUDA context that
+ * loads the library (the device's primary context, or a context the caller
+ * created and made current) holds its own copy of the array; the first call in
+ * a context looks up that copy's address; make it before any stream capture.
  * Every call on a device uses the same array, so calls that overlap on the GPU
  * race. This entry point has no counterpart in the reference. */
 int dsa_indexer_fwd_noalloc(const void* x, const void* qr, const void* wq_b, const void* w_proj,

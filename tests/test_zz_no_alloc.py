@@ -6,7 +6,8 @@ latency-critical path that must not pay for cudaMalloc/cudaFree -- by keeping
 the q and w intermediates in a fixed 128 MiB array inside the library. These
 tests call it through the C ABI and check that two calls in a row (different
 inputs, same shared array) return exactly the indices of the workspace-taking
-entry point, dsa_indexer_fwd, and that an oversized request is rejected.
+entry point, dsa_indexer_fwd, and that the documented token limit is exact:
+at 650 candidates per token, 25,981 tokens succeed and 25,982 are rejected.
 
 This file is named so that pytest collects it last.
 """
@@ -38,54 +39,61 @@ def _max_tokens():
     return lo
 
 
-def _inputs(seed, dev, batch=8, seqlen=2600):
+def _inputs(seed, dev, batch=8, seqlen=2600, start_pos=0):
     torch.manual_seed(seed)
     args, freqs_cis, kv_cache, ratio = ix.get_init_inputs(device="cpu")
     model = ix.ModelNew(args, freqs_cis, kv_cache, ratio)
-    x = torch.randn(batch, seqlen, args.dim, dtype=torch.bfloat16, device=dev)
-    qr = torch.randn(batch, seqlen, args.q_lora_rank, dtype=torch.bfloat16, device=dev)
-    fc = torch.view_as_real(freqs_cis[:seqlen])
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn(batch, seqlen, args.dim, dtype=torch.bfloat16, device=dev, generator=g)
+    qr = torch.randn(batch, seqlen, args.q_lora_rank, dtype=torch.bfloat16, device=dev,
+                     generator=g)
+    T = (start_pos + seqlen) // ratio
+    if batch <= kv_cache.shape[0]:
+        kv = kv_cache.to(dev)
+    else:
+        kv = torch.randn(batch, T, args.index_head_dim, dtype=torch.bfloat16, device=dev,
+                         generator=g)
+    fc = torch.view_as_real(freqs_cis[start_pos:start_pos + seqlen])
     return dict(
         x=x, qr=qr, wq=model.wq_b.weight.detach().to(dev).contiguous(),
         wp=model.weights_proj.weight.detach().to(dev).contiguous(),
         cos=fc[..., 0].contiguous().to(dev), sin=fc[..., 1].contiguous().to(dev),
-        kv=kv_cache.to(dev), batch=batch, seqlen=seqlen,
+        kv=kv, batch=batch, seqlen=seqlen, start_pos=start_pos, T=T, K=min(128, T),
         w_scale=model.softmax_scale * model.n_heads ** -0.5)
 
 
-def _common_args(d, out):
-    T = d["seqlen"] // 4
+def _head(d, out):
     return [d["x"].data_ptr(), d["qr"].data_ptr(), d["wq"].data_ptr(), d["wp"].data_ptr(),
             d["cos"].data_ptr(), d["sin"].data_ptr(), d["kv"].data_ptr(), d["kv"].stride(0),
-            out.data_ptr()], T
+            out.data_ptr()]
 
 
 def _tail(d, stream):
-    return [d["batch"], d["seqlen"], 1024, 256, 16, 64, 32, 128, 0, 4, 0,
+    return [d["batch"], d["seqlen"], 1024, 256, 16, 64, 32, 128, d["start_pos"], 4, 0,
             ctypes.c_float(d["w_scale"]), stream]
+
+
+def _out(d, dev):
+    return torch.empty(d["batch"], d["seqlen"], d["K"], dtype=torch.int64, device=dev)
 
 
 def _with_workspace(d, dev):
     lib = _native.lib()
-    T = d["seqlen"] // 4
-    out = torch.empty(d["batch"], d["seqlen"], min(128, T), dtype=torch.int64, device=dev)
-    head, _ = _common_args(d, out)
-    nbytes = lib.dsa_indexer_workspace_bytes(d["batch"], d["seqlen"], 16, 64, T, min(128, T))
+    out = _out(d, dev)
+    nbytes = lib.dsa_indexer_workspace_bytes(d["batch"], d["seqlen"], 16, 64, d["T"], d["K"])
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    tail = _tail(d, stream)
-    st = lib.dsa_indexer_fwd(*head, ws.data_ptr(), nbytes, *tail)
+    st = lib.dsa_indexer_fwd(*_head(d, out), ws.data_ptr(), nbytes, *_tail(d, stream))
     assert st == 0, st
     return out
 
 
 def _no_alloc(d, dev):
     lib = _native.lib()
-    T = d["seqlen"] // 4
-    out = torch.empty(d["batch"], d["seqlen"], min(128, T), dtype=torch.int64, device=dev)
-    head, _ = _common_args(d, out)
+    out = _out(d, dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    st = lib.dsa_indexer_fwd_noalloc(*head, *_tail(d, stream))
+    st = lib.dsa_indexer_fwd_noalloc(*_head(d, out), *_tail(d, stream))
     assert st == 0, st
     return out
 
@@ -104,13 +112,26 @@ def test_no_alloc_matches_workspace_entry_point(cuda_device):
     assert _native.device_error(dev.index) == 0
 
 
-def test_no_alloc_rejects_requests_beyond_its_array(cuda_device):
+def test_no_alloc_limit_is_exact(cuda_device):
+    """At 650 candidates (the reference's count) the array holds exactly
+    _max_tokens() tokens: that many succeed with the indices of the workspace
+    entry point, one more is rejected before any launch. The tokens are spread
+    over the batch (seqlen 1 at start_pos 2599, so every token has 650
+    candidates)."""
     dev = cuda_device
-    d = _inputs(3, dev, batch=1, seqlen=64)
+    n = _max_tokens()
+    assert n == 25981, n  # the documented limit
+    d = _inputs(4, dev, batch=n, seqlen=1, start_pos=2599)
+    assert d["T"] == 650
+    want = _with_workspace(d, dev)
+    got = _no_alloc(d, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert _native.device_error(dev.index) == 0
+    del d, want, got
+    e = _inputs(5, dev, batch=n + 1, seqlen=1, start_pos=2599)
     lib = _native.lib()
-    out = torch.empty(1, 64, 16, dtype=torch.int64, device=dev)
-    head, _ = _common_args(d, out)
+    out = _out(e, dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    tail = _tail(d, stream)
-    tail[0], tail[1] = 1, _max_tokens() + 1   # batch, seqlen beyond the fixed array
-    assert lib.dsa_indexer_fwd_noalloc(*head, *tail) == DSA_ERR_WORKSPACE
+    assert lib.dsa_indexer_workspace_bytes(n + 1, 1, 16, 64, 650, 128) > LIMIT_BYTES
+    assert lib.dsa_indexer_fwd_noalloc(*_head(e, out), *_tail(e, stream)) == DSA_ERR_WORKSPACE
