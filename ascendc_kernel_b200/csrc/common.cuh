@@ -68,6 +68,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0u;
 }
 
+// Non-blocking test of the same phase (never parks the thread).
+__device__ __forceinline__ bool mbar_ready(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
 // Wait for the phase of `bar` with parity `parity` to complete. Returns false
 // (and raises *abort) when the wait runs past kWaitLimitNs or when another
 // role of the CTA has already aborted.

@@ -14,16 +14,22 @@
 //               32 KB, double buffered) and 128-row kv chunks (16 KB, 3 stages)
 //   warp 1      tcgen05: D[128 kv rows x 256 (t,h)] = KV_chunk . Q^T (K = 64)
 //               into one of two 256-column TMEM buffers
-//   warps 2..9  two epilogue warpgroups (tokens 0-7 / 8-15 of the unit). A
+//   warps 4..11 two epilogue warpgroups (tokens 0-7 / 8-15 of the unit). A
 //               thread owns one kv row: it loads its 16 head values per token,
 //               certifies each bf16 rounding against the accumulation bound
 //               (numerics.cuh; elements that cannot be certified are
-//               recomputed exactly by the whole warp in fp64), runs the
-//               relu / *w / head-sum chain and stores a unique 32-bit key
-//               (orderable bf16 score << 16 | 0xFFFF - k) in shared memory.
-//               After the last chunk each warp selects the top-K of two tokens
-//               with an 8-bit radix select over the keys and a register
-//               bitonic sort, and writes the int64 indices.
+//               recomputed exactly by the whole warp), runs the relu / *w /
+//               head-sum chain and stores the orderable 16-bit score of every
+//               valid candidate in one of two key buffers in shared memory.
+//   warps 2, 3, 12..15  top-K selection, one unit behind the epilogue: the
+//               six warps take the unit's eight token pairs in turn (a binary
+//               search over the 16 score bits, ties by ascending k, then a
+//               register bitonic sort), write the int64 indices and hand the
+//               key buffer back once all eight pairs are done. The selection of
+//               one unit thus overlaps the score chain of the next.
+// Registers: 512 threads launch with 128 each; the epilogue warpgroups raise
+// theirs to 144 and the other two lower theirs to 112 (setmaxnreg), which adds
+// up to the launch's 65,536.
 #include "common.cuh"
 #include "host_util.h"
 #include "numerics.cuh"
@@ -39,26 +45,36 @@ constexpr int kChunk = 128;              // kv rows per MMA
 constexpr int kMaxT = 1024;              // candidates held in smem per token
 constexpr int kMaxK = 256;               // top-k held in registers
 constexpr int kKVStages = 3;
-constexpr int kThreads = 320;
+constexpr int kThreads = 512;  // warps 0 TMA, 1 MMA, 2-3 and 12-15 selection, 4-11 epilogue
+constexpr int kSelWarps = 6;
+constexpr int kEpiWarp0 = 4;
+constexpr int kLaunchRegs = 128;   // 65536 / kThreads: the kernel must compile to exactly this
+constexpr int kEpiRegs = 144;      // epilogue warpgroups (1, 2)
+constexpr int kOtherRegs = 112;    // warpgroups 0 (producers, 2 selection warps) and 3 (selection)
+static_assert(2 * kEpiRegs + 2 * kOtherRegs == 4 * kLaunchRegs, "register split must add up");
 constexpr uint32_t kTmemCols = 512;
 
 constexpr int kQBytes = kQRows * 128;    // 32 KB
 constexpr int kKVBytes = kChunk * 128;   // 16 KB
+constexpr int kKeyBufBytes = kTB * kMaxT * 2;                 // 32 KB: [16 tokens][1024] u16
 constexpr int kOffQ = 0;
 constexpr int kOffKV = kOffQ + 2 * kQBytes;                   // 65536
-constexpr int kOffKeys = kOffKV + kKVStages * kKVBytes;       // 114688
-constexpr int kOffQN = kOffKeys + kTB * kMaxT * 4;            // 180224
+constexpr int kOffKeys = kOffKV + kKVStages * kKVBytes;       // 114688: two key buffers
+constexpr int kOffQN = kOffKeys + 2 * kKeyBufBytes;           // 180224
 constexpr int kOffW = kOffQN + kQRows * 4;                    // 181248
-constexpr int kOffSel = kOffW + kQRows * 4;                   // 182272: per warp hist + sel
-constexpr int kHistCopies = 4;                                // histogram + drain queue space
-constexpr int kSelBytes = kHistCopies * 256 * 4 + kMaxK * 4;  // 5 KB per warp
-constexpr int kOffNV = kOffSel + 8 * kSelBytes;               // 223232: [16] int
+constexpr int kOffRq = kOffW + kQRows * 4;                    // 182272: drain queue per epilogue warp
+constexpr int kRqBytes = 4096;  // also the warp's selection scratch between units
+static_assert(kRqBytes >= 2 * kMaxK * 4, "drain queue region too small for selection scratch");
+constexpr int kOffSel = kOffRq + 8 * kRqBytes;                // 223232: two [kMaxK] lists per selection warp
+constexpr int kSelBytes = 2 * kMaxK * 4;
+constexpr int kOffNV = kOffSel + kSelWarps * kSelBytes;       // 227328: [16] int
 constexpr int kOffWP = kOffNV + kTB * 4;                      // [256] w as bf16x2 {w, w}
 constexpr int kOffPS = kOffWP + kQRows * 4;                   // [256] prmt selector
 constexpr int kOffBar = kOffPS + kQRows * 4;
-constexpr int kNumBars = 2 + 2 + 2 * kKVStages + 2 + 2;
+constexpr int kNumBars = 2 + 2 + 2 * kKVStages + 2 + 2 + 2 + 2;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmem = kOffMisc + 16 + 1024;
+static_assert(kSmem <= 232448, "shared memory above the 227 KB per-block limit");
 
 // Accumulation bound for one K = 64 accumulator (4 MMA steps at 3 fp32 ulps
 // each, in units of ||q|| * ||kv||).
@@ -274,11 +290,11 @@ __device__ __forceinline__ uint32_t ord_to_bf16(uint32_t ord) {
 
 // Queued pairs, 32 at a time: exact recomputation of the heads whose interval
 // is open and can be positive (spread one per lane), then the exact score
-// chain, one lane per pair; writes the key (or, with gs, the bf16 score to
-// gs[token slot * gld + k]).
+// chain, one lane per pair; writes the orderable score (or, with gs, the bf16
+// score to gs[token slot * gld + k]).
 __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs, const float* qn,
                                          const uint8_t* kv_stages, const float* wv,
-                                         const uint32_t* wpk, uint32_t* keys, uint16_t* gs,
+                                         const uint32_t* wpk, uint16_t* keys, uint16_t* gs,
                                          int64_t gld, int lane) {
   __syncwarp();
   for (int i0 = 0; i0 < n; i0 += 32) {
@@ -334,7 +350,7 @@ __device__ __noinline__ void drain_queue(uint32_t* rq, int n, const uint8_t* qs,
       if (gs)
         gs[tt * gld + k] = static_cast<uint16_t>(ord_to_bf16(key >> 16));
       else
-        keys[tt * kMaxT + k] = key;
+        keys[tt * kMaxT + k] = static_cast<uint16_t>(key >> 16);
     }
   }
   __syncwarp();
@@ -407,7 +423,7 @@ __device__ __forceinline__ void sort_and_store2(const uint32_t* sel0, int nsel0,
   }
 }
 
-// Top-Ksel of the n keys in `keys` (smem, in candidate order) by one warp, for
+// Top-Ksel of the n orderable scores in `keys` (smem, in candidate order) by one warp, for
 // two tokens at once (their steps interleaved; the second may be absent:
 // n1 = 0, out1 = nullptr). A key is (orderable score << 16) | (0xFFFF - k), so
 // the order is score descending, then k ascending. The keys are held in
@@ -416,7 +432,7 @@ __device__ __forceinline__ void sort_and_store2(const uint32_t* sel0, int nsel0,
 // scoring exactly thr are taken in k order (the order they are stored in) up
 // to Ksel. The selected keys are then compacted and sorted.
 template <int R>
-__device__ __forceinline__ void warp_topk2_r(const uint32_t* keys0, int n0, const uint32_t* keys1,
+__device__ __forceinline__ void warp_topk2_r(const uint16_t* keys0, int n0, const uint16_t* keys1,
                                              int n1, int K_out, uint32_t* sel0, uint32_t* sel1,
                                              int64_t* out0, int64_t* out1, int64_t offset,
                                              int lane) {
@@ -426,8 +442,9 @@ __device__ __forceinline__ void warp_topk2_r(const uint32_t* keys0, int n0, cons
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = r * 32 + lane;
-    v[r] = i < n0 ? keys0[i] : 0u;  // a real key scores >= 1, padding scores 0
-    u[r] = i < n1 ? keys1[i] : 0u;
+    // key = orderable score << 16 | (0xFFFF - k); a real key scores >= 1, padding 0
+    v[r] = i < n0 ? (static_cast<uint32_t>(keys0[i]) << 16) | (0xFFFFu - i) : 0u;
+    u[r] = i < n1 ? (static_cast<uint32_t>(keys1[i]) << 16) | (0xFFFFu - i) : 0u;
   }
   const bool all0 = n0 <= ksel0, all1 = n1 <= ksel1;
   uint32_t thr0 = 0, thr1 = 0;
@@ -483,18 +500,168 @@ __device__ __forceinline__ void warp_topk2_r(const uint32_t* keys0, int n0, cons
   __syncwarp();
 }
 
-__device__ void warp_topk2(const uint32_t* keys0, int n0, const uint32_t* keys1, int n1, int K_out,
+// One token's top-Ksel, the same steps as warp_topk2_r for a single list (used
+// for lists longer than 512, where two lists' keys would not fit the selection
+// warps' registers).
+template <int R>
+__device__ __forceinline__ void warp_bitonic_desc1(uint32_t (&v)[R], int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= 32) {
+        const int rs = stride >> 5;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          if ((r & rs) == 0) {
+            const bool desc_block = ((r * 32 + lane) & size) == 0;
+            const uint32_t a = v[r], b = v[r | rs];
+            if (desc_block ? (a < b) : (a > b)) {
+              v[r] = b;
+              v[r | rs] = a;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int i = r * 32 + lane;
+          const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, v[r], stride);
+          const bool keep_max = (((i & stride) == 0) == ((i & size) == 0));
+          v[r] = keep_max ? max(v[r], o) : min(v[r], o);
+        }
+      }
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void sort_and_store1(const uint32_t* sel, int nsel, int64_t* out,
+                                                int K_out, int64_t offset, int lane) {
+  uint32_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < nsel ? sel[i] : 0u;
+  }
+  warp_bitonic_desc1<R>(v, lane);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    if (i < K_out)
+      out[i] = i < nsel ? static_cast<int64_t>(0xFFFFu - (v[r] & 0xFFFFu)) + offset
+                        : static_cast<int64_t>(-1);
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void warp_topk1_r(const uint16_t* keys, int n, int K_out,
+                                             uint32_t* sel, int64_t* out, int64_t offset,
+                                             int lane) {
+  const int ksel = n < K_out ? n : K_out;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  uint32_t v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < n ? (static_cast<uint32_t>(keys[i]) << 16) | (0xFFFFu - i) : 0u;
+  }
+  const bool all = n <= ksel;
+  uint32_t thr = 0;
+  int need = 0;
+  if (!all) {
+    for (int bit = 15; bit >= 0; --bit) {
+      const uint32_t cand = (thr | (1u << bit)) << 16;
+      int c = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) c += v[r] >= cand ? 1 : 0;
+      c = static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
+      if (c >= ksel) thr |= 1u << bit;
+    }
+    const uint32_t above = (thr + 1) << 16;
+    int c = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) c += v[r] >= above ? 1 : 0;
+    need = ksel - static_cast<int>(__reduce_add_sync(0xFFFFFFFFu, static_cast<unsigned>(c)));
+  }
+  int base = 0, ties = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const bool valid = r * 32 + lane < n;
+    const uint32_t sc = v[r] >> 16;
+    const bool tie = !all && valid && sc == thr;
+    const uint32_t tb = __ballot_sync(0xFFFFFFFFu, tie);
+    const bool take = valid && (all || sc > thr || (tie && ties + __popc(tb & lt_mask) < need));
+    ties += __popc(tb);
+    const uint32_t bm = __ballot_sync(0xFFFFFFFFu, take);
+    if (take) sel[base + __popc(bm & lt_mask)] = v[r];
+    base += __popc(bm);
+  }
+  __syncwarp();
+  if (K_out <= 128)
+    sort_and_store1<4>(sel, base, out, K_out, offset, lane);
+  else
+    sort_and_store1<8>(sel, base, out, K_out, offset, lane);
+  __syncwarp();
+}
+
+__device__ void warp_topk2(const uint16_t* keys0, int n0, const uint16_t* keys1, int n1, int K_out,
                            uint32_t* sel0, uint32_t* sel1, int64_t* out0, int64_t* out1,
                            int64_t offset, int lane) {
   const int n = n0 > n1 ? n0 : n1;
-  if (n <= 256)
+  if (n <= 256) {
     warp_topk2_r<8>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
-  else if (n <= 512)
+  } else if (n <= 512) {
     warp_topk2_r<16>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
-  else if (n <= 768)
-    warp_topk2_r<24>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
-  else
-    warp_topk2_r<32>(keys0, n0, keys1, n1, K_out, sel0, sel1, out0, out1, offset, lane);
+  } else if (n <= 768) {
+    warp_topk1_r<24>(keys0, n0, K_out, sel0, out0, offset, lane);
+    if (out1) warp_topk1_r<24>(keys1, n1, K_out, sel0, out1, offset, lane);
+  } else {
+    warp_topk1_r<32>(keys0, n0, K_out, sel0, out0, offset, lane);
+    if (out1) warp_topk1_r<32>(keys1, n1, K_out, sel0, out1, offset, lane);
+  }
+}
+
+// Selection of token pair g of the CTA's sequence (unit lu = g / 8 of this
+// CTA, tokens 2 (g % 8) and 2 (g % 8) + 1): waits until the unit's keys are
+// written (every lane acquires them; immediate when they already are), selects
+// both tokens, writes their indices and arrives on the key buffer's release
+// barrier. Returns false past the CTA's last unit or when the wait gave up.
+__device__ __forceinline__ bool select_pair(const Params& p, int g, const uint8_t* smem,
+                                         uint64_t* keys_full, uint64_t* keys_empty,
+                                         uint32_t* sel0, uint32_t* sel1, volatile int* abort_flag,
+                                         int lane) {
+  constexpr int kPairs = kTB / 2;
+  const int lu = g / kPairs, pr = g % kPairs;
+  const int u = blockIdx.x + lu * gridDim.x;
+  if (u >= p.units) return false;
+  const int b = u % p.B;
+  const int64_t t0 = static_cast<int64_t>(p.n_tb - 1 - u / p.B) * kTB;
+  const int kb = lu & 1;
+  if (!__all_sync(0xFFFFFFFFu, mbar_wait(&keys_full[kb], (lu >> 1) & 1, abort_flag, p.err,
+                                         DSA_DEVERR_IX_WAIT)))
+    return false;
+  const uint16_t* kbuf = reinterpret_cast<const uint16_t*>(smem + kOffKeys + kb * kKeyBufBytes);
+  // the pair's two tokens, selected together (the second may lie past the end)
+  const int tt = 2 * pr;
+  const int64_t tok = t0 + tt;
+  if (tok < p.S) {
+    const bool two = tok + 1 < p.S;
+    int64_t* out0 = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
+    warp_topk2(kbuf + tt * kMaxT, static_cast<int>(n_valid(p, tok)), kbuf + (tt + 1) * kMaxT,
+               two ? static_cast<int>(n_valid(p, tok + 1)) : 0, p.K, sel0, sel1, out0,
+               two ? out0 + p.K : nullptr, p.offset, lane);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&keys_empty[kb]);
+  return true;
+}
+
+// Next pair of the CTA's selection sequence (one atomic per warp).
+__device__ __forceinline__ int grab_pair(int* next, int lane) {
+  int g = 0;
+  if (lane == 0) g = atomicAdd(next, 1);
+  return __shfl_sync(0xFFFFFFFFu, g, 0);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -510,8 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_empty = kv_full + kKVStages;      // [3], 2 arrivals
   uint64_t* acc_full = kv_empty + kKVStages;     // [2]
   uint64_t* acc_empty = acc_full + 2;            // [2], 256 arrivals
+  uint64_t* keys_full = acc_empty + 2;           // [2], 256 arrivals (epilogue threads)
+  uint64_t* keys_empty = keys_full + 2;          // [2], 8 arrivals (one per token pair)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  int* sel_next = reinterpret_cast<int*>(smem + kOffMisc + 8);  // next token pair to select
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -526,7 +696,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 256);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&keys_full[i], 256);
+      mbar_init(&keys_empty[i], kTB / 2);
+    }
     *abort_flag = 0;
+    *sel_next = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -554,89 +729,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     return static_cast<int>((nv + kChunk - 1) / kChunk);
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      int lu = 0, gc = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
-        int b;
-        int64_t t0;
-        unit_of(u, b, t0);
-        const int nch = unit_chunks(t0);
-        const int qb = lu & 1;
-        if (!mbar_wait(&q_empty[qb], ((lu >> 1) & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT))
-          break;
-        mbar_arrive_expect_tx(&q_full[qb], kQBytes);
-        tma_load_2d(smem + kOffQ + qb * kQBytes, &tm_q, 0,
-                    static_cast<int32_t>((static_cast<int64_t>(b) * p.S + t0) * kHeads), &q_full[qb]);
-        for (int c = 0; c < nch; ++c, ++gc) {
-          const int s = gc % kKVStages;
-          if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
-                         DSA_DEVERR_IX_WAIT)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
-          tma_load_2d(smem + kOffKV + s * kKVBytes, &tm_kv, 0,
-                      static_cast<int32_t>(b * p.kv_rows_per_batch + c * kChunk), &kv_full[s]);
-        }
-      }
-      if (lu > 0) mbar_drain(&q_full[(lu - 1) & 1], ((lu - 1) >> 1) & 1);
-      if (lu > 1) mbar_drain(&q_full[(lu - 2) & 1], ((lu - 2) >> 1) & 1);
-      for (int i = (gc > kKVStages ? gc - kKVStages : 0); i < gc; ++i)
-        mbar_drain(&kv_full[i % kKVStages], (i / kKVStages) & 1);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(128, kQRows, 0, 0);
-      int lu = 0, gc = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
-        int b;
-        int64_t t0;
-        unit_of(u, b, t0);
-        const int nch = unit_chunks(t0);
-        const int qb = lu & 1;
-        // Every unit runs the full q-buffer handshake, even one without chunks.
-        if (!mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT)) break;
-        const uint32_t qaddr = smem_u32(smem + kOffQ + qb * kQBytes);
-        for (int c = 0; c < nch; ++c, ++gc) {
-          const int s = gc % kKVStages;
-          const int ab = gc & 1;
-          if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
-                         DSA_DEVERR_IX_WAIT) ||
-              !mbar_wait(&acc_empty[ab], ((gc >> 1) & 1) ^ 1, abort_flag, p.err,
-                         DSA_DEVERR_IX_WAIT)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t kvaddr = smem_u32(smem + kOffKV + s * kKVBytes);
-#pragma unroll
-          for (int k4 = 0; k4 < kDim / 16; ++k4) {
-            const uint64_t ad = make_smem_desc(kvaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
-            const uint64_t bd = make_smem_desc(qaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
-            umma_bf16(tmem + static_cast<uint32_t>(ab) * 256u, ad, bd, idesc, k4 > 0 ? 1u : 0u);
-          }
-          umma_commit(&acc_full[ab]);
-        }
-      }
-      if (gc > 0) mbar_drain(&acc_full[(gc - 1) & 1], ((gc - 1) >> 1) & 1);
-      if (gc > 1) mbar_drain(&acc_full[(gc - 2) & 1], ((gc - 2) >> 1) & 1);
-    }
-  } else {
+  // Roles by warpgroup, each region under its own register limit (setmaxnreg
+  // is warpgroup-wide; see kLaunchRegs): warpgroups 1 and 2 are the epilogue,
+  // warpgroups 0 and 3 the producers and the selection warps.
+  if ((warp >> 2) == 1 || (warp >> 2) == 2) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kEpiRegs));
     // ------------------------------------------------------------ epilogue
-    const int wg = (warp - 2) >> 2;          // tokens [8 wg, 8 wg + 8) of the unit
-    const int t_in = threadIdx.x - 64 - 128 * wg;  // 0..127
+    const int wg = (warp - kEpiWarp0) >> 2;  // tokens [8 wg, 8 wg + 8) of the unit
+    const int t_in = threadIdx.x - 32 * kEpiWarp0 - 128 * wg;  // 0..127
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;     // kv row of the chunk = TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int ew = warp - 2;                 // 0..7, selection warp id
+    const int ew = warp - kEpiWarp0;         // 0..7
     float* qn = reinterpret_cast<float*>(smem + kOffQN);
     float* wv = reinterpret_cast<float*>(smem + kOffW);
-    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + kOffKeys);
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kOffSel + ew * kSelBytes);
-    uint32_t* sel = hist + kHistCopies * 256;
+    // this warp's queue of pairs that need an exact recomputation; empty
+    // between units, when it serves as selection scratch
+    uint32_t* rq = reinterpret_cast<uint32_t*>(smem + kOffRq + ew * kRqBytes);
     bool ok = true;
     int lu = 0, gc = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++lu) {
@@ -645,6 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       unit_of(u, b, t0);
       const int nch = unit_chunks(t0);
       const int qb = lu & 1;
+      const int kb = lu & 1;
+      uint16_t* keys = reinterpret_cast<uint16_t*>(smem + kOffKeys + kb * kKeyBufBytes);
       const uint8_t* qs = smem + kOffQ + qb * kQBytes;
       uint16_t* gs = p.scores ? p.scores + (static_cast<int64_t>(b) * p.S + t0) * p.score_ld
                               : nullptr;
@@ -667,13 +778,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err,
                                              DSA_DEVERR_IX_WAIT));
       if (ok) qn[qrow] = row_norm64(qs, qrow);
-      // Early exits below always fall through to the CTA-wide barrier 3, which
-      // both warpgroups reach the same number of times.
+      // the key buffer of this unit is free once the selection of unit lu - 2 is done
+      if (ok && gs == nullptr)
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&keys_empty[kb], ((lu >> 1) & 1) ^ 1, abort_flag,
+                                               p.err, DSA_DEVERR_IX_WAIT));
       ok = named_bar_and(1 + wg, 128, ok);
-      // the selection scratch of this warp is idle until the selection: it holds
-      // the queue of pairs that need an exact recomputation
-      uint32_t* rq = hist;
-      constexpr int kRqCap = kSelBytes / 4 / kRqWords;
+      constexpr int kRqCap = kRqBytes / 4 / kRqWords;
       const uint8_t* kv_stages = smem + kOffKV;
       // queued pairs are drained every second chunk (or when the queue would
       // overflow, or at the unit's end); a thread releases a kv stage only after
@@ -700,6 +810,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int tl = 0; tl < 8; tl += 2) {
             // two tokens per TMEM load: 32 columns = 2 tokens x 16 heads
             const int tt0 = wg * 8 + tl;
+            // nothing to do when all 32 rows of this warp lie past both tokens'
+            // valid candidates (the unit's last chunk under the causal mask)
+            if (c * kChunk + quarter * 32 >= max(nvs[tt0], nvs[tt0 + 1])) continue;
             uint32_t r[32];
             tmem_ld_32x32b_x32(tmem + lane_off + static_cast<uint32_t>(ab * 256 + tt0 * 16), r);
             // both tokens' interval chains first (one basic block, so their
@@ -784,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   gs[tt * p.score_ld + k] = static_cast<uint16_t>(tlo[j]);
                 } else {
                   const uint32_t ord = (tlo[j] & 0x8000u) ? (~tlo[j] & 0xFFFFu) : (tlo[j] | 0x8000u);
-                  keys[tt * kMaxT + k] = (ord << 16) | (0xFFFFu - static_cast<uint32_t>(k));
+                  keys[tt * kMaxT + k] = static_cast<uint16_t>(ord);
                 }
               }
             }
@@ -810,26 +923,105 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // the warpgroup leaves the unit together: its per-token arrays are rewritten next
       ok = named_bar_and(1 + wg, 128, ok);
-      if (ok) mbar_arrive(&q_empty[qb]);
-      if (gs) {  // scores go to global memory; the top-k runs in its own kernel
-        if (!ok) break;
-        continue;
+      if (!ok) break;
+      mbar_arrive(&q_empty[qb]);
+      // this thread's keys of the unit are written (with gs the scores went to
+      // global memory and the top-k runs in its own kernel)
+      if (gs == nullptr) mbar_arrive(&keys_full[kb]);
+    }
+    // after the last unit: help select the pairs still pending
+    if (ok && p.scores == nullptr) {
+      while (select_pair(p, grab_pair(sel_next, lane), smem, keys_full, keys_empty, rq, rq + kMaxK,
+                         abort_flag, lane)) {
       }
-      // all keys of the unit are written
-      if (!named_bar_and(3, 256, ok)) break;
-      {
-        // the warp's two tokens, selected together (the second may lie past the end)
-        const int tt = ew * 2;
-        const int64_t tok = t0 + tt;
-        if (tok < p.S) {
-          const bool two = tok + 1 < p.S;
-          int64_t* out0 = p.out + (static_cast<int64_t>(b) * p.S + tok) * p.K;
-          warp_topk2(keys + tt * kMaxT, static_cast<int>(n_valid(p, tok)), keys + (tt + 1) * kMaxT,
-                     two ? static_cast<int>(n_valid(p, tok + 1)) : 0, p.K, sel, hist,
-                     out0, two ? out0 + p.K : nullptr, p.offset, lane);
+    }
+    } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kOtherRegs));
+    if (warp == 0) {
+      if (lane == 0) {
+        int lu = 0, gc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
+          int b;
+          int64_t t0;
+          unit_of(u, b, t0);
+          const int nch = unit_chunks(t0);
+          const int qb = lu & 1;
+          if (!mbar_wait(&q_empty[qb], ((lu >> 1) & 1) ^ 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT))
+            break;
+          mbar_arrive_expect_tx(&q_full[qb], kQBytes);
+          tma_load_2d(smem + kOffQ + qb * kQBytes, &tm_q, 0,
+                      static_cast<int32_t>((static_cast<int64_t>(b) * p.S + t0) * kHeads), &q_full[qb]);
+          for (int c = 0; c < nch; ++c, ++gc) {
+            const int s = gc % kKVStages;
+            if (!mbar_wait(&kv_empty[s], ((gc / kKVStages) & 1) ^ 1, abort_flag, p.err,
+                           DSA_DEVERR_IX_WAIT)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+            tma_load_2d(smem + kOffKV + s * kKVBytes, &tm_kv, 0,
+                        static_cast<int32_t>(b * p.kv_rows_per_batch + c * kChunk), &kv_full[s]);
+          }
+        }
+        if (lu > 0) mbar_drain(&q_full[(lu - 1) & 1], ((lu - 1) >> 1) & 1);
+        if (lu > 1) mbar_drain(&q_full[(lu - 2) & 1], ((lu - 2) >> 1) & 1);
+        for (int i = (gc > kKVStages ? gc - kKVStages : 0); i < gc; ++i)
+          mbar_drain(&kv_full[i % kKVStages], (i / kKVStages) & 1);
+      }
+    } else if (warp == 1) {
+      if (lane == 0) {
+        constexpr uint32_t idesc = make_idesc_bf16_f32(128, kQRows, 0, 0);
+        int lu = 0, gc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.units; u += gridDim.x, ++lu) {
+          int b;
+          int64_t t0;
+          unit_of(u, b, t0);
+          const int nch = unit_chunks(t0);
+          const int qb = lu & 1;
+          // Every unit runs the full q-buffer handshake, even one without chunks.
+          if (!mbar_wait(&q_full[qb], (lu >> 1) & 1, abort_flag, p.err, DSA_DEVERR_IX_WAIT)) break;
+          const uint32_t qaddr = smem_u32(smem + kOffQ + qb * kQBytes);
+          for (int c = 0; c < nch; ++c, ++gc) {
+            const int s = gc % kKVStages;
+            const int ab = gc & 1;
+            if (!mbar_wait(&kv_full[s], (gc / kKVStages) & 1, abort_flag, p.err,
+                           DSA_DEVERR_IX_WAIT) ||
+                !mbar_wait(&acc_empty[ab], ((gc >> 1) & 1) ^ 1, abort_flag, p.err,
+                           DSA_DEVERR_IX_WAIT)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t kvaddr = smem_u32(smem + kOffKV + s * kKVBytes);
+  #pragma unroll
+            for (int k4 = 0; k4 < kDim / 16; ++k4) {
+              const uint64_t ad = make_smem_desc(kvaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
+              const uint64_t bd = make_smem_desc(qaddr + k4 * 32, 16u, 1024u, kLayoutSW128);
+              umma_bf16(tmem + static_cast<uint32_t>(ab) * 256u, ad, bd, idesc, k4 > 0 ? 1u : 0u);
+            }
+            umma_commit(&acc_full[ab]);
+          }
+        }
+        if (gc > 0) mbar_drain(&acc_full[(gc - 1) & 1], ((gc - 1) >> 1) & 1);
+        if (gc > 1) mbar_drain(&acc_full[(gc - 2) & 1], ((gc - 2) >> 1) & 1);
+      }
+    } else {
+      // ----------------------------------------------------------- selection
+      // One unit behind the epilogue. The units' token pairs form one sequence
+      // (unit lu holds pairs 8 lu .. 8 lu + 7), handed out by a shared counter
+      // to these six warps and, once their last unit is done, to the epilogue
+      // warps; per pair the taker writes the two tokens' indices and arrives on
+      // the key buffer's release barrier (8 arrivals per unit).
+      if (p.scores == nullptr) {
+        const int sw = warp < kEpiWarp0 ? warp - 2 : warp - kEpiWarp0 - 6;  // 0..5
+        uint32_t* sel0 = reinterpret_cast<uint32_t*>(smem + kOffSel + sw * kSelBytes);
+        uint32_t* sel1 = sel0 + kMaxK;
+        while (select_pair(p, grab_pair(sel_next, lane), smem, keys_full, keys_empty, sel0, sel1,
+                           abort_flag, lane)) {
         }
       }
-      if (!named_bar_and(3, 256, ok)) break;
     }
   }
 
@@ -892,6 +1084,18 @@ int launch_score_topk(const void* q, const void* w, const void* kv, int64_t kv_b
   p.err = err;
   st = set_max_dynamic_smem(reinterpret_cast<const void*>(score_topk_kernel), kSmem);
   if (st != DSA_OK) return st;
+  {
+    // the setmaxnreg split assumes exactly kLaunchRegs per thread at launch; a
+    // build with fewer would make the epilogue's increase wait forever
+    static int regs = -1;
+    if (regs < 0) {
+      cudaFuncAttributes fa;
+      st = cuda_status(cudaFuncGetAttributes(&fa, score_topk_kernel));
+      if (st != DSA_OK) return st;
+      regs = fa.numRegs;
+    }
+    if (regs != kLaunchRegs) return DSA_ERR_UNSUPPORTED;
+  }
   const int grid = p.units < di.num_sms ? p.units : di.num_sms;
   score_topk_kernel<<<grid, kThreads, kSmem, stream>>>(tm_q, tm_kv, p);
   return cuda_status(cudaGetLastError());
