@@ -48,6 +48,16 @@ SIGNATURES = {
                                        _c_void_p, _c_void_p, _i64, _c_void_p, _i64, _i64, _i32,
                                        _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i64, _f32,
                                        _c_void_p]),
+    "dsa_indexer_fp8_quant_rows": (_i32, [_c_void_p, _i64, _i64, _i64, _i32, _c_void_p,
+                                          _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "dsa_indexer_score_topk_fp8": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                          _c_void_p, _i64, _i64, _i32, _i32, _i64, _i32, _i64,
+                                          _i32, _i64, _c_void_p]),
+    "dsa_indexer_fp8_workspace_bytes": (_size_t, [_i64, _i64, _i32, _i32, _i64]),
+    "dsa_indexer_fwd_fp8": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                   _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _size_t,
+                                   _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _i32,
+                                   _i64, _f32, _c_void_p]),
     "dsa_chain_workspace_bytes": (_size_t, [_i64, _i64, _i32, _i32, _i64]),
     "dsa_chain_fwd": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                              _c_void_p, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,

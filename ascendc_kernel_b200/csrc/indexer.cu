@@ -356,3 +356,135 @@ extern "C" int dsa_chain_fwd(const void* x, const void* qr, const void* wq_b, co
   return dsa::launch_sa_long_mask(q, kv, mask, words, offset, sink, out, batch, seqlen,
                                   attn_heads, n_kv, softmax_scale, s);
 }
+
+// ---------------------------------------------------------------- fp8 path
+namespace dsa {
+int launch_fp8_quant_rows(const void* src, int64_t rows, int64_t rows_per_group,
+                          int64_t group_stride, void* dst, float* scale, const void* w,
+                          float* w_out, cudaStream_t stream);
+int launch_score_fp8(const void* q8, const float* wq, const void* k8, const float* ks,
+                     int64_t* out, float* scores, int64_t batch, int64_t seqlen, int64_t n_cand,
+                     int topk, int64_t start_pos, int ratio, int64_t offset, cudaStream_t stream);
+namespace {
+struct Fp8Layout {
+  size_t q, w, q8, wq, k8, ks, bytes;
+};
+Fp8Layout fp8_layout(int64_t batch, int64_t seqlen, int n_heads, int head_dim, int64_t n_cand) {
+  const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(seqlen);
+  const size_t qe = rows * n_heads * head_dim;
+  const size_t kr = static_cast<size_t>(batch) * static_cast<size_t>(n_cand);
+  Fp8Layout l;
+  l.q = front_bytes(n_heads, head_dim, static_cast<int64_t>(rows));
+  l.w = l.q + align256(qe * 2);
+  l.q8 = l.w + align256(rows * n_heads * 2);
+  l.wq = l.q8 + align256(qe);
+  l.k8 = l.wq + align256(rows * n_heads * 4);
+  l.ks = l.k8 + align256(kr * head_dim);
+  l.bytes = l.ks + align256(kr * 4);
+  return l;
+}
+
+int check_score_fp8(const void* q8, const float* wq, const void* k8, const float* ks,
+                    const int64_t* out, int64_t batch, int64_t seqlen, int n_heads, int head_dim,
+                    int64_t n_cand, int topk, int64_t start_pos, int ratio) {
+  if (!q8 || !wq || !k8 || !ks || !out || batch < 0 || seqlen < 0 || n_cand < 0 || topk < 0 ||
+      start_pos < 0 || ratio <= 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (n_heads != kScoreHeads || head_dim != kHeadDim) return DSA_ERR_UNSUPPORTED;
+  if (topk > n_cand) return DSA_ERR_INVALID_ARGUMENT;
+  if (!score_fused(n_cand, topk)) return DSA_ERR_UNSUPPORTED;
+  if (batch * seqlen * kScoreHeads > kMaxRowsTma || batch * n_cand > kMaxRowsTma)
+    return DSA_ERR_UNSUPPORTED;
+  if (!aligned16(q8) || !aligned16(wq) || !aligned16(k8) || !aligned16(ks) || !aligned16(out))
+    return DSA_ERR_MISALIGNED;
+  return DSA_OK;
+}
+}  // namespace
+}  // namespace dsa
+
+extern "C" int dsa_indexer_fp8_quant_rows(const void* x, int64_t rows, int64_t rows_per_group,
+                                          int64_t group_stride, int head_dim, void* y,
+                                          float* scale, const void* w, float* w_out,
+                                          void* stream) {
+  if (!x || !y || rows < 0 || rows_per_group <= 0 || group_stride < 0 ||
+      ((w == nullptr) != (w_out == nullptr)))
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (head_dim != dsa::kHeadDim) return DSA_ERR_UNSUPPORTED;
+  if (rows_per_group < rows && group_stride < rows_per_group * dsa::kHeadDim)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (!dsa::aligned16(x) || !dsa::aligned16(y) || (group_stride % 8) != 0)
+    return DSA_ERR_MISALIGNED;
+  if (rows == 0) return DSA_OK;
+  return dsa::launch_fp8_quant_rows(x, rows, rows_per_group, group_stride, y, scale, w, w_out,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_indexer_score_topk_fp8(const void* q8, const float* wq, const void* k8,
+                                          const float* ks, int64_t* out, float* scores,
+                                          int64_t batch, int64_t seqlen, int n_heads,
+                                          int head_dim, int64_t n_cand, int topk,
+                                          int64_t start_pos, int ratio, int64_t offset,
+                                          void* stream) {
+  const int st = dsa::check_score_fp8(q8, wq, k8, ks, out, batch, seqlen, n_heads, head_dim,
+                                      n_cand, topk, start_pos, ratio);
+  if (st != DSA_OK || batch == 0 || seqlen == 0 || topk == 0) return st;
+  return dsa::launch_score_fp8(q8, wq, k8, ks, out, scores, batch, seqlen, n_cand, topk,
+                               start_pos, ratio, offset, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t dsa_indexer_fp8_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads,
+                                                  int head_dim, int64_t n_cand) {
+  if (batch <= 0 || seqlen <= 0 || n_heads <= 0 || head_dim <= 0 || n_cand <= 0) return 0;
+  return dsa::fp8_layout(batch, seqlen, n_heads, head_dim, n_cand).bytes;
+}
+
+extern "C" int dsa_indexer_fwd_fp8(const void* x, const void* qr, const void* wq_b,
+                                   const void* w_proj, const float* cos_tab,
+                                   const float* sin_tab, const void* kv_cache,
+                                   int64_t kv_batch_stride, int64_t* out, void* workspace,
+                                   size_t workspace_bytes, int64_t batch, int64_t seqlen, int dim,
+                                   int q_lora_rank, int n_heads, int head_dim, int rope_dim,
+                                   int index_topk, int64_t start_pos, int ratio, int64_t offset,
+                                   float w_scale, void* stream) {
+  if (batch < 0 || seqlen < 0 || index_topk <= 0 || ratio <= 0 || start_pos < 0 || !kv_cache)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seqlen == 0) return DSA_OK;
+  const int64_t rows = batch * seqlen;
+  const int64_t n_cand = (start_pos + seqlen) / ratio;
+  const int topk = static_cast<int>(index_topk < n_cand ? index_topk : n_cand);
+  if (topk <= 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (kv_batch_stride < n_cand * head_dim) return DSA_ERR_INVALID_ARGUMENT;
+  if (!dsa::aligned16(kv_cache) || kv_batch_stride % 8 != 0) return DSA_ERR_MISALIGNED;
+  const dsa::Fp8Layout l = dsa::fp8_layout(batch, seqlen, n_heads, head_dim, n_cand);
+  if (workspace == nullptr || workspace_bytes < l.bytes ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return DSA_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* q = ws + l.q;
+  void* w = ws + l.w;
+  void* q8 = ws + l.q8;
+  float* wq = reinterpret_cast<float*>(ws + l.wq);
+  void* k8 = ws + l.k8;
+  float* ks = reinterpret_cast<float*>(ws + l.ks);
+  int st = dsa::check_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
+                            rope_dim, seqlen);
+  if (st != DSA_OK) return st;
+  st = dsa::check_wproj(x, w_proj, w, rows, dim, n_heads);
+  if (st != DSA_OK) return st;
+  st = dsa::check_score_fp8(q8, wq, k8, ks, out, batch, seqlen, n_heads, head_dim, n_cand, topk,
+                            start_pos, ratio);
+  if (st != DSA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
+                      rope_dim, seqlen, ws, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, ws, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_fp8_quant_rows(q, rows * n_heads, rows * n_heads, 0, q8, nullptr, w, wq, s);
+  if (st != DSA_OK) return st;
+  st = dsa::launch_fp8_quant_rows(kv_cache, batch * n_cand, n_cand, kv_batch_stride, k8, ks,
+                                  nullptr, nullptr, s);
+  if (st != DSA_OK) return st;
+  return dsa::launch_score_fp8(q8, wq, k8, ks, out, nullptr, batch, seqlen, n_cand, topk,
+                               start_pos, ratio, offset, s);
+}

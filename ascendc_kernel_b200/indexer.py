@@ -111,8 +111,15 @@ class ModelNew(nn.Module):
     """Drop-in for ``Model`` of reference/task2_v0_ref.py:106-144."""
 
     def __init__(self, args, freqs_cis: torch.Tensor, kv_cache: torch.Tensor,
-                 compress_ratio: int = 4):
+                 compress_ratio: int = 4, fp8_index: bool = False):
+        """``fp8_index=True`` selects the fp8 index path that ModelArgs.dtype =
+        "fp8" / scale_fmt = "ue8m0" declares (reference/task2_v0_ref.py:25-26):
+        q and kv_cache rows are Hadamard-rotated and quantized to e4m3 with
+        power-of-two scales and scored on the fp8 tensor cores
+        (dsa_indexer_fwd_fp8). The default is the reference's bf16 path
+        (reference/task2_v0_ref.py:123-144), bit-exact."""
         super().__init__()
+        self.fp8_index = bool(fp8_index)
         self.dim = args.dim
         self.n_heads = args.index_n_heads
         self.n_local_heads = args.index_n_heads // world_size
@@ -173,7 +180,9 @@ class ModelNew(nn.Module):
         assert self.n_local_heads == 16 and self.head_dim == 64, \
             "kernel specialised to index_n_heads == 16, index_head_dim == 64"
         assert self.rope_head_dim % 2 == 0 and self.rope_head_dim <= self.head_dim
-        assert T <= 8192, "kernels support up to 8192 candidates"
+        assert T <= (1024 if self.fp8_index else 8192), "candidate count above the kernels' limit"
+        if self.fp8_index:
+            assert K <= 256, "the fp8 path selects up to 256 candidates"
         assert K >= 1, "need at least one candidate (end_pos >= compress_ratio)"
         kv = self.kv_cache
         assert kv.is_cuda and kv.dtype == torch.bfloat16 and kv.device == dev
@@ -184,13 +193,20 @@ class ModelNew(nn.Module):
         qr = qr.contiguous()
         wq, wp = self._weights_on(dev)
         cos, sin = self._rope_tables(start_pos, seqlen, dev)
-        nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim, T, K)
+        if self.fp8_index:
+            nbytes = lib().dsa_indexer_fp8_workspace_bytes(bsz, seqlen, self.n_heads,
+                                                           self.head_dim, T)
+            fn = "dsa_indexer_fwd_fp8"
+        else:
+            nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim,
+                                                       T, K)
+            fn = "dsa_indexer_fwd"
         ws = self._workspace(nbytes, dev)
         out = torch.empty(bsz, seqlen, K, dtype=torch.int64, device=dev)
         w_scale = self.softmax_scale * self.n_heads ** -0.5
         stream = torch.cuda.current_stream(dev).cuda_stream
         with torch.cuda.device(dev):
-            call("dsa_indexer_fwd", x.data_ptr(), qr.data_ptr(), wq.data_ptr(), wp.data_ptr(),
+            call(fn, x.data_ptr(), qr.data_ptr(), wq.data_ptr(), wp.data_ptr(),
                  cos.data_ptr(), sin.data_ptr(), kv.data_ptr(), kv.stride(0), out.data_ptr(),
                  ws.data_ptr(), ws.numel(), bsz, seqlen, self.dim, self.q_lora_rank,
                  self.n_heads, self.head_dim, self.rope_head_dim, self.index_topk, start_pos,
@@ -250,6 +266,50 @@ def score_topk(q: torch.Tensor, w: torch.Tensor, kv_cache: torch.Tensor, batch: 
              kv_cache.data_ptr(), kv_cache.stride(0), out.data_ptr(), batch, seqlen, 16, 64,
              n_cand, topk, start_pos, ratio, offset, ws.data_ptr(), nbytes, stream)
     return out
+
+
+def fp8_quant_rows(x: torch.Tensor, w: torch.Tensor = None):
+    """Hadamard rotation + ue8m0 e4m3 quantization of 64-wide bf16 rows
+    (dsa_indexer_fp8_quant_rows). x [..., 64] bf16 contiguous. Returns (y uint8
+    [rows, 64] e4m3 bits, scale f32 [rows]) and, with w (bf16, one per row),
+    also w * scale (f32 [rows])."""
+    x = x.contiguous()
+    rows = x.numel() // 64
+    y = torch.empty(rows, 64, dtype=torch.uint8, device=x.device)
+    sc = torch.empty(rows, dtype=torch.float32, device=x.device)
+    wo = None
+    if w is not None:
+        w = w.contiguous()
+        assert w.numel() == rows and w.dtype == torch.bfloat16
+        wo = torch.empty(rows, dtype=torch.float32, device=x.device)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        call("dsa_indexer_fp8_quant_rows", x.data_ptr(), rows, rows, 0, 64, y.data_ptr(),
+             sc.data_ptr(), w.data_ptr() if w is not None else None,
+             wo.data_ptr() if wo is not None else None, stream)
+    return (y, sc, wo) if w is not None else (y, sc)
+
+
+def score_topk_fp8(q8: torch.Tensor, wq: torch.Tensor, k8: torch.Tensor, ks: torch.Tensor,
+                   batch: int, seqlen: int, n_cand: int, topk: int, start_pos: int, ratio: int,
+                   offset: int, want_scores: bool = False):
+    """fp8 scores and top-k (dsa_indexer_score_topk_fp8). q8 [batch*seqlen*16, 64]
+    uint8, wq [batch*seqlen, 16] f32, k8 [batch*n_cand, 64] uint8, ks [batch*n_cand]
+    f32. Returns int64 [batch, seqlen, topk] (and the f32 scores [batch*seqlen,
+    n_cand], NaN where masked, with want_scores)."""
+    dev = q8.device
+    out = torch.empty(batch, seqlen, topk, dtype=torch.int64, device=dev)
+    scores = None
+    if want_scores:
+        scores = torch.full((batch * seqlen, n_cand), float("nan"), dtype=torch.float32,
+                            device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        call("dsa_indexer_score_topk_fp8", q8.contiguous().data_ptr(), wq.contiguous().data_ptr(),
+             k8.contiguous().data_ptr(), ks.contiguous().data_ptr(), out.data_ptr(),
+             scores.data_ptr() if scores is not None else None, batch, seqlen, 16, 64, n_cand,
+             topk, start_pos, ratio, offset, stream)
+    return (out, scores) if want_scores else out
 
 
 def _make_args():

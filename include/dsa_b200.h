@@ -181,6 +181,55 @@ int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b, const void*
                     int q_lora_rank, int n_heads, int head_dim, int rope_dim, int index_topk,
                     int64_t start_pos, int ratio, int64_t offset, float w_scale, void* stream);
 
+/* ---- fp8 index path: ModelArgs.dtype = "fp8", scale_fmt = "ue8m0"
+ * (reference/task2_v0_ref.py:25-26; declared there, unused by the bf16 v0
+ * path). Definition after DeepSeek-V3.2-Exp's published indexer
+ * (inference/model.py Indexer.forward, inference/kernel.py act_quant and
+ * fp8_index), one quantization block per 64-wide head row:
+ *   h = bf16(FWHT64(x) * 2^-3)          Walsh-Hadamard rotation, fp32 butterflies
+ *                                       over strides 1, 2, ..., 32
+ *   s = 2^ceil(log2(fp32(max(amax(h), 1e-4) / 448)))      (ue8m0 scale)
+ *   y = e4m3(h / s)                     RNE, |h / s| <= 448
+ *   score[t,k] = ks[k] * sum_h relu(fp32(q8[t,h] . k8[k])) * wq[t,h]
+ *                (wq = w * qs, the head sum an fp32 fma chain in ascending h)
+ *   top-k, mask, -1 and offset as dsa_indexer_score_topk.
+ * The q8 . k8 products run on tcgen05.mma kind::f8f6f4 with fp32 accumulate. */
+
+/* Rotates and quantizes `rows` 64-wide bf16 rows: row r of group g = r /
+ * rows_per_group at x + g*group_stride + (r % rows_per_group)*64 (group_stride
+ * in elements, a multiple of 8; rows_per_group >= rows for one contiguous
+ * block). y [rows, 64] e4m3 contiguous; scale [rows] f32 or NULL; with w (bf16
+ * [rows]) w_out[r] = w[r] * s[r] (exact). Supported: head_dim == 64. */
+int dsa_indexer_fp8_quant_rows(const void* x, int64_t rows, int64_t rows_per_group,
+                               int64_t group_stride, int head_dim, void* y, float* scale,
+                               const void* w, float* w_out, void* stream);
+
+/* Scores and top-k on quantized rows: q8 [batch*seqlen*n_heads, 64] e4m3, wq
+ * [batch*seqlen, n_heads] f32, k8 [batch*n_cand, 64] e4m3, ks [batch*n_cand] f32,
+ * out [batch*seqlen, topk] int64; scores (NULL or [batch*seqlen, n_cand] f32)
+ * receives the fp32 score of every valid candidate (others untouched).
+ * Supported: n_heads == 16, head_dim == 64, topk <= 256, n_cand <= 1024. */
+int dsa_indexer_score_topk_fp8(const void* q8, const float* wq, const void* k8, const float* ks,
+                               int64_t* out, float* scores, int64_t batch, int64_t seqlen,
+                               int n_heads, int head_dim, int64_t n_cand, int topk,
+                               int64_t start_pos, int ratio, int64_t offset, void* stream);
+
+/* Workspace bytes of dsa_indexer_fwd_fp8 (256-byte aligned). */
+size_t dsa_indexer_fp8_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim,
+                                       int64_t n_cand);
+
+/* The fp8 variant of dsa_indexer_fwd, same arguments: the bf16 projections and
+ * RoPE (bit-exact, as dsa_indexer_fwd), then the rotation and quantization of q
+ * (with wq = w * qs) and of kv_cache rows 0 .. n_cand-1 of every batch, then
+ * dsa_indexer_score_topk_fp8. Same limits as that call. */
+int dsa_indexer_fwd_fp8(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                        const float* cos_tab, const float* sin_tab, const void* kv_cache,
+                        int64_t kv_batch_stride, int64_t* out, void* workspace,
+                        size_t workspace_bytes, int64_t batch, int64_t seqlen, int dim,
+                        int q_lora_rank, int n_heads, int head_dim, int rope_dim, int index_topk,
+                        int64_t start_pos, int ratio, int64_t offset, float w_scale,
+                        void* stream);
+
 /* dsa_indexer_fwd for callers that cannot allocate device memory at call
  * time -- plug-ins whose host framework owns all device memory and forbids
  * allocating inside an operator, or latency-critical paths where a

@@ -38,6 +38,10 @@ _SIGS = {
     "oracle_scale_bf16": (None, [_vp, _i64, _f32]),
     "oracle_index_topk": (None, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i64,
                                  _i32, _i64, _i32, _i64]),
+    "oracle_e4m3_array": (None, [_vp, _i64, _vp]),
+    "oracle_fp8_quant_rows": (None, [_vp, _i64, _vp, _vp]),
+    "oracle_index_topk_fp8": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64,
+                                     _i32, _i64, _i32, _i64]),
 }
 
 
@@ -167,4 +171,62 @@ def indexer_fwd(x, qr, wq, wp, cos, sin, kv, *, n_heads, head_dim, rope_dim, ind
     idx = idx.reshape(B, S, K)
     if want_intermediates:
         return idx, {"q": q, "w": w, "scores": scores}
+    return idx
+
+
+# ----------------------------------------------------------- fp8 index path
+def e4m3(x: np.ndarray) -> np.ndarray:
+    """fp32 -> float8_e4m3fn bits (RNE, saturating to +-448)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, dtype=np.uint8)
+    lib().oracle_e4m3_array(_p(x), x.size, _p(y))
+    return y
+
+
+def fp8_quant_rows(x: np.ndarray):
+    """Hadamard rotation + ue8m0 e4m3 quantization of 64-wide bf16 rows.
+    x [..., 64] u16. Returns (y u8 [rows, 64], scale f32 [rows])."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    rows = x.size // 64
+    y = np.empty((rows, 64), dtype=np.uint8)
+    s = np.empty(rows, dtype=np.float32)
+    lib().oracle_fp8_quant_rows(_p(x), rows, _p(y), _p(s))
+    return y, s
+
+
+def index_topk_fp8(q8, wq, k8, ks, batch, seqlen, n_heads, head_dim, n_cand, topk, start_pos,
+                   ratio, offset, want_scores=False):
+    """fp8 scores + mask + top-k; q8 [B*S*H, Dh] u8, wq [B*S*H] f32, k8 [B*T, Dh] u8,
+    ks [B*T] f32. Returns (idx [B*S, K] int64, scores f32 [B*S, T] or None)."""
+    q8 = np.ascontiguousarray(q8, dtype=np.uint8)
+    wq = np.ascontiguousarray(wq, dtype=np.float32)
+    k8 = np.ascontiguousarray(k8, dtype=np.uint8)
+    ks = np.ascontiguousarray(ks, dtype=np.float32)
+    out = np.empty((batch * seqlen, topk), dtype=np.int64)
+    scores = np.empty((batch * seqlen, n_cand), dtype=np.float32) if want_scores else None
+    lib().oracle_index_topk_fp8(_p(q8), _p(wq), _p(k8), _p(ks), _p(out),
+                                _p(scores) if want_scores else None, batch, seqlen, n_heads,
+                                head_dim, n_cand, topk, start_pos, ratio, offset)
+    return out, scores
+
+
+def indexer_fwd_fp8(x, qr, wq, wp, cos, sin, kv, *, n_heads, head_dim, rope_dim, index_topk,
+                    start_pos, ratio, offset, w_scale, want_intermediates=False):
+    """The fp8 index path end to end: the bf16 projections and RoPE of
+    indexer_fwd, then rotation + quantization of q (weights times the q rows'
+    scales) and of kv rows 0 .. T-1 of every batch, then index_topk_fp8."""
+    B, S, _ = x.shape
+    T = (start_pos + S) // ratio
+    K = min(index_topk, T)
+    q = linear_bf16(qr.reshape(B * S, -1), wq)
+    q = rope(q, cos, sin, n_heads, head_dim, rope_dim, S)
+    w = scale_bf16(linear_bf16(x.reshape(B * S, -1), wp), w_scale)
+    q8, qs = fp8_quant_rows(q.reshape(-1, head_dim))
+    wqs = ((w.reshape(-1).astype(np.uint32) << 16).view(np.float32) * qs).astype(np.float32)
+    k8, ks = fp8_quant_rows(np.ascontiguousarray(kv[:, :T]).reshape(-1, head_dim))
+    idx, scores = index_topk_fp8(q8, wqs, k8, ks, B, S, n_heads, head_dim, T, K, start_pos,
+                                 ratio, offset, want_scores=want_intermediates)
+    idx = idx.reshape(B, S, K)
+    if want_intermediates:
+        return idx, {"q": q, "w": w, "q8": q8, "wq": wqs, "k8": k8, "ks": ks, "scores": scores}
     return idx

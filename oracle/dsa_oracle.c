@@ -335,3 +335,141 @@ void oracle_index_topk(const uint16_t* q, const uint16_t* w, const uint16_t* kv,
     free(kvt);
   }
 }
+
+/* ------------------------------------------------------------ fp8 index path
+ * The fp8 variant that ModelArgs.dtype = "fp8", scale_fmt = "ue8m0" declares
+ * (reference/task2_v0_ref.py:25-26) and the reference's bf16 v0 path never
+ * uses. Restated from the published indexer of DeepSeek-V3.2-Exp
+ * (inference/model.py, Indexer.forward: rotate_activation, act_quant with
+ * scale_fmt, weights * q_scale, fp8_index; inference/kernel.py, act_quant and
+ * fp8_index), with one quantization block per 64-wide head row:
+ *   h = bf16(FWHT64(x) * 2^-3)   Walsh-Hadamard in fp32, butterflies (a+b, a-b)
+ *                                over strides 1, 2, 4, ..., 32
+ *   s = 2^ceil(log2(fp32(max(max|h|, 1e-4) / 448)))      (ue8m0 scale)
+ *   y = e4m3(h / s)              RNE, |h / s| <= 448
+ *   score[t,k] = ks[k] * sum_h relu(fp32(q8[t,h] . k8[k])) * wq[t,h]
+ *     with the e4m3 dot product exact (fp64) then rounded once to fp32, the
+ *     head sum an fp32 fma chain in ascending h, wq = fp32(w) * qs.
+ *   Mask, top-k order (score desc, k asc, -0 == +0), -1 and offset as
+ *   oracle_index_topk.
+ */
+
+/* fp32 -> e4m3 (float8_e4m3fn) bits, RNE, saturating to +-448; NaN -> 0x7F. */
+uint8_t oracle_e4m3_from_f32(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+  const float a = fabsf(f);
+  if (a != a) return 0x7Fu;
+  if (a >= 448.0f) return (uint8_t)(sign | 0x7Eu);
+  if (a < 0.015625f) { /* below 2^-6: multiples of 2^-9 (subnormals) */
+    const int m = (int)rintf(a * 512.0f); /* a * 2^9 exact; rintf is RNE */
+    return (uint8_t)(sign | (uint8_t)m);  /* m == 8 encodes 2^-6 */
+  }
+  int e;
+  const float fr = frexpf(a, &e); /* a = fr * 2^e, fr in [0.5, 1) */
+  int q = (int)rintf((fr * 2.0f - 1.0f) * 8.0f); /* exact: 24-bit significand */
+  int ex = e - 1 + 7;
+  if (q == 8) {
+    q = 0;
+    ex += 1;
+  }
+  return (uint8_t)(sign | (uint8_t)(ex << 3) | (uint8_t)q);
+}
+
+static inline double e4m3_to_f64(uint8_t b) {
+  const int s = b >> 7, ex = (b >> 3) & 15, m = b & 7;
+  double v;
+  if (ex == 0)
+    v = ldexp((double)m, -9);
+  else
+    v = ldexp((double)(8 + m), ex - 10);
+  return s ? -v : v;
+}
+
+static inline float bf16_round_f32(float f) { return bf2f(f2bf(f)); }
+
+/* x [rows, 64] bf16 -> y [rows, 64] e4m3 bits, scale [rows] (may be NULL). */
+void oracle_fp8_quant_rows(const uint16_t* x, int64_t rows, uint8_t* y, float* scale) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    float h[64];
+    for (int i = 0; i < 64; ++i) h[i] = bf2f(x[r * 64 + i]);
+    for (int len = 1; len < 64; len <<= 1)
+      for (int i = 0; i < 64; i += 2 * len)
+        for (int j = i; j < i + len; ++j) {
+          const float a = h[j], b = h[j + len];
+          h[j] = a + b;
+          h[j + len] = a - b;
+        }
+    float amax = 0.0f;
+    for (int i = 0; i < 64; ++i) {
+      h[i] = bf16_round_f32(h[i] * 0.125f);
+      const float ah = fabsf(h[i]);
+      if (ah > amax) amax = ah;
+    }
+    if (amax < 1e-4f) amax = 1e-4f;
+    const float q = amax / 448.0f;
+    uint32_t qu;
+    memcpy(&qu, &q, 4);
+    const int e = (int)((qu >> 23) & 0xFFu) - 127 + ((qu & 0x7FFFFFu) != 0u ? 1 : 0);
+    const float s = ldexpf(1.0f, e);
+    for (int i = 0; i < 64; ++i) y[r * 64 + i] = oracle_e4m3_from_f32(h[i] / s);
+    if (scale) scale[r] = s;
+  }
+}
+
+/* q8 [B*S*H, Dh] e4m3, wq [B*S*H] f32, k8 [B*T, Dh] e4m3, ks [B*T] f32;
+ * out [B*S, K] int64; scores_out (NULL or [B*S, T] f32, masked = -inf). */
+void oracle_index_topk_fp8(const uint8_t* q8, const float* wq, const uint8_t* k8,
+                           const float* ks, int64_t* out, float* scores_out, int64_t B,
+                           int64_t S, int H, int Dh, int64_t T, int K, int64_t start_pos,
+                           int ratio, int64_t offset) {
+#pragma omp parallel
+  {
+    uint64_t* keys = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)T);
+    double* qd = (double*)malloc(sizeof(double) * (size_t)H * Dh);
+#pragma omp for schedule(dynamic, 8)
+    for (int64_t bt = 0; bt < B * S; ++bt) {
+      const int64_t b = bt / S, t = bt % S;
+      int64_t nv = T;
+      if (start_pos == 0) {
+        nv = (t + 1) / ratio;
+        if (nv > T) nv = T;
+      }
+      for (int i = 0; i < H * Dh; ++i) qd[i] = e4m3_to_f64(q8[bt * H * Dh + i]);
+      for (int64_t k = 0; k < nv; ++k) {
+        const uint8_t* kr = k8 + (b * T + k) * Dh;
+        double kd[256];
+        for (int d = 0; d < Dh; ++d) kd[d] = e4m3_to_f64(kr[d]);
+        float acc = 0.0f;
+        for (int h = 0; h < H; ++h) {
+          double dot = 0.0; /* exact: e4m3 products and their sum fit in fp64 */
+          for (int d = 0; d < Dh; ++d) dot += qd[h * Dh + d] * kd[d];
+          float df = (float)dot;
+          if (!(df > 0.0f)) df = 0.0f;
+          acc = fmaf(df, wq[bt * H + h], acc);
+        }
+        float sc = acc * ks[b * T + k];
+        if (scores_out) scores_out[bt * T + k] = sc;
+        uint32_t u;
+        memcpy(&u, &sc, 4);
+        if (u == 0x80000000u) u = 0;
+        const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        keys[k] = ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)k);
+      }
+      if (scores_out)
+        for (int64_t k = nv; k < T; ++k) scores_out[bt * T + k] = -INFINITY;
+      qsort(keys, (size_t)nv, sizeof(uint64_t), cmp_desc_u64);
+      int64_t* o = out + bt * K;
+      for (int j = 0; j < K; ++j)
+        o[j] = j < nv ? (int64_t)(0xFFFFFFFFu - (uint32_t)(keys[j] & 0xFFFFFFFFu)) + offset : -1;
+    }
+    free(keys);
+    free(qd);
+  }
+}
+
+void oracle_e4m3_array(const float* x, int64_t n, uint8_t* y) {
+  for (int64_t i = 0; i < n; ++i) y[i] = oracle_e4m3_from_f32(x[i]);
+}

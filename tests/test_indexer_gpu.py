@@ -92,6 +92,24 @@ def test_qproj_slicing_edge_cases(cuda_device, k, mode):
     assert _native.device_error(dev.index) == 0
 
 
+@pytest.mark.parametrize("k", [64, 512, 1024])
+@pytest.mark.parametrize("mode", ["normal", "wide", "special"])
+def test_wproj_edge_cases(cuda_device, k, mode):
+    """w projection (fp64 sums in ascending k) on ragged row counts, exponent
+    ranges wider than fp32's, zero / subnormal / overflowing rows: bit-exact."""
+    gen = torch.Generator().manual_seed(k * 5 + len(mode))
+    rows = 300  # not a multiple of the 64-row work unit
+    x = _edge_rows(mode, rows, k, gen)
+    wp = _edge_rows(mode, 16, k, gen)
+    dev = cuda_device
+    scale = 64 ** -0.5 * 16 ** -0.5
+    w = ix.wproj(x.to(dev), wp.to(dev), scale)
+    want = oracle.scale_bf16(oracle.linear_bf16(to_u16(x), to_u16(wp)), scale)
+    got = to_u16(w)
+    assert np.array_equal(got, want), int((got != want).sum())
+    assert _native.device_error(dev.index) == 0
+
+
 @pytest.mark.parametrize("p", ["p_", "d_"])
 def test_forward_golden_equals_oracle(golden_dir, cuda_device, p):
     g, c = golden(golden_dir, p)
