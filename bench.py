@@ -390,6 +390,33 @@ def bench_indexer(dev, world, cpu: bool):
                         "score_kernel_tflops": s_tfl, "score_kernel_tensor_frac": s_tfl / tc,
                         "peak_source": f"hbm {hbm_kind}, bf16 {tc_kind} burst"},
            "shape": "x[8,2600,1024] qr[8,2600,256] kv_cache[8,650,64] top-128 per GPU"}
+    # fp8 index path (ModelArgs.dtype "fp8" / ue8m0) on the same inputs and weights
+    model_8 = ix.ModelNew(args, freqs.to(dev), kvc.to(dev), ratio, fp8_index=True)
+    model_8.load_state_dict(model.state_dict())
+    for _ in range(3):
+        out8 = model_8(xd, qrd, sp, off)
+    torch.cuda.synchronize()
+    barrier()
+    ms8 = max_over_ranks(cuda_timed(lambda: model_8(xd, qrd, sp, off), 10, warm=2))
+    w8 = w.reshape(-1)
+    q8, _, wq8 = ix.fp8_quant_rows(q.reshape(-1, 64), w8)
+    k8, ks8 = ix.fp8_quant_rows(kv_d[:, :IX_T].contiguous().reshape(-1, 64))
+    s8_ms = cuda_timed(lambda: ix.score_topk_fp8(q8, wq8, k8, ks8, IX_B, IX_S, IX_T, IX_K, 0, 4,
+                                                 0), 10, warm=2)
+    s8_bytes = IX_B * IX_S * 16 * (64 + 4) + IX_B * IX_T * (64 + 4) + IX_B * IX_S * IX_K * 8
+    fp8_tc = 2 * tc  # dense fp8 tensor rate: twice the measured bf16 burst (no measured fp8 figure)
+    s8_tfl = flops_score / (s8_ms * 1e-3) / 1e12
+    res["fp8"] = {
+        "us_per_call": ms8 * 1e3, "tokens_per_s": world * IX_B * IX_S / (ms8 * 1e-3),
+        "score_kernel_us": s8_ms * 1e3,
+        "roofline": {"bound": "mixed (warp top-k selection)",
+                     "score_kernel_algorithmic_flops": flops_score,
+                     "score_kernel_tflops": s8_tfl, "score_kernel_fp8_tensor_frac": s8_tfl / fp8_tc,
+                     "score_kernel_algorithmic_bytes": s8_bytes,
+                     "score_kernel_hbm_frac": s8_bytes / (s8_ms * 1e-3) / 1e9 / hbm,
+                     "peak_source": f"fp8 = 2 x bf16 {tc_kind} burst; hbm {hbm_kind}"},
+        "form": "ModelNew(..., fp8_index=True): bf16 projections, Hadamard + ue8m0 e4m3 "
+                "quantization of q and kv_cache, tcgen05 kind::f8f6f4 scores, warp top-k"}
     if cpu:
         from oracle import v0_torch
 
@@ -402,6 +429,22 @@ def bench_indexer(dev, world, cpu: bool):
                                "kind": "port", "tokens_per_s": IX_B * IX_S / s,
                                "sample": f"full configs[2] shape x {runs} calls, torch v0 "
                                          "Model.forward"}
+        # fp8 path against the oracle's restatement, batch 0 (2,600 tokens)
+        import oracle
+
+        fc = torch.view_as_real(freqs[:IX_S])
+        want8 = oracle.indexer_fwd_fp8(
+            u16(x[:1]), u16(qr[:1]), u16(wqc), u16(wpc), fc[..., 0].contiguous().numpy(),
+            fc[..., 1].contiguous().numpy(), u16(kvc[:1]), n_heads=16, head_dim=64, rope_dim=32,
+            index_topk=IX_K, start_pos=0, ratio=4, offset=0,
+            w_scale=model.softmax_scale * model.n_heads ** -0.5)
+        got8 = out8[:1].cpu().numpy()
+        res["fp8"]["parity_vs_oracle"] = {
+            "rows": int(IX_S), "rows_equal": int((got8 == want8).all(-1).sum()),
+            "sets_equal": int(sum(set(a.tolist()) == set(b.tolist())
+                                  for a, b in zip(got8[0], want8[0]))),
+            "sample": "batch 0 of configs[2]; the oracle rounds each e4m3 dot product "
+                      "once, the tensor cores' fp32 accumulation may differ in the last bit"}
     return res
 
 
@@ -821,6 +864,19 @@ def run_profile_case(args):
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": "ix", "batch": 8, "steps": args.warmup + args.steps}))
         return
+    if args.profile == "ix8":
+        # the fp8 index path at configs[2] (ModelNew(..., fp8_index=True)), W + K forwards
+        from ascendc_kernel_b200 import indexer as ix
+
+        torch.manual_seed(42)
+        a, fr, kvc, ratio = ix.get_init_inputs(device=str(dev))
+        model = ix.ModelNew(a, fr, kvc, ratio, fp8_index=True)
+        inp = ix.get_inputs(device=str(dev))
+        for _ in range(args.warmup + args.steps):
+            model(*inp)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "ix8", "batch": 8, "steps": args.warmup + args.steps}))
+        return
     if args.profile in ("chain", "fchain"):
         # configs[3] at batch args.batch (1: ~0.9 GB on the device): indexer top-2048,
         # then the long-pool SparseAttention over its indices ("chain": two calls,
@@ -861,7 +917,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa", "ix", "chain", "fchain", "sk"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix", "ix8", "chain", "fchain", "sk"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()
