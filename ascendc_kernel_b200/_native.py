@@ -58,6 +58,9 @@ SIGNATURES = {
                                    _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _size_t,
                                    _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _i32,
                                    _i64, _f32, _c_void_p]),
+    "dsa_kv_cache_write": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                  _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
+                                  _i64, _i32, _c_void_p]),
     "dsa_chain_workspace_bytes": (_size_t, [_i64, _i64, _i32, _i32, _i64]),
     "dsa_chain_fwd": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                              _c_void_p, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,

@@ -488,3 +488,36 @@ extern "C" int dsa_indexer_fwd_fp8(const void* x, const void* qr, const void* wq
   return dsa::launch_score_fp8(q8, wq, k8, ks, out, nullptr, batch, seqlen, n_cand, topk,
                                start_pos, ratio, offset, s);
 }
+
+// ------------------------------------------------------------ kv_cache writer
+namespace dsa {
+int launch_kv_writer(const void* x, const void* wk, const float* g, const float* b,
+                     const float* cos_t, const float* sin_t, void* kv, int64_t kv_bstride,
+                     int64_t batch, int64_t seqlen, int dim, int rope_dim, int64_t start_pos,
+                     int ratio, cudaStream_t stream);
+}  // namespace dsa
+
+extern "C" int dsa_kv_cache_write(const void* x, const void* wk, const float* ln_weight,
+                                  const float* ln_bias, const float* cos_tab,
+                                  const float* sin_tab, void* kv_cache, int64_t kv_batch_stride,
+                                  int64_t kv_rows, int64_t batch, int64_t seqlen, int dim,
+                                  int head_dim, int rope_dim, int64_t start_pos, int ratio,
+                                  void* stream) {
+  if (!x || !wk || !ln_weight || !ln_bias || !kv_cache || batch < 0 || seqlen < 0 || dim <= 0 ||
+      start_pos < 0 || ratio <= 0 || rope_dim < 0 || (rope_dim & 1) || kv_rows < 0)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (rope_dim > 0 && (!cos_tab || !sin_tab)) return DSA_ERR_INVALID_ARGUMENT;
+  if (head_dim != dsa::kHeadDim || rope_dim > head_dim || dim % 64 != 0 || 128 % ratio != 0)
+    return DSA_ERR_UNSUPPORTED;
+  if (start_pos % ratio != 0) return DSA_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || seqlen < ratio) return DSA_OK;  // no complete block
+  if ((start_pos + seqlen) / ratio > kv_rows || kv_batch_stride < kv_rows * head_dim)
+    return DSA_ERR_INVALID_ARGUMENT;
+  if (batch * seqlen > dsa::kMaxRowsTma) return DSA_ERR_UNSUPPORTED;
+  if (!dsa::aligned16(x) || !dsa::aligned16(wk) || !dsa::aligned16(kv_cache) ||
+      kv_batch_stride % 8 != 0)
+    return DSA_ERR_MISALIGNED;
+  return dsa::launch_kv_writer(x, wk, ln_weight, ln_bias, cos_tab, sin_tab, kv_cache,
+                               kv_batch_stride, batch, seqlen, dim, rope_dim, start_pos, ratio,
+                               static_cast<cudaStream_t>(stream));
+}

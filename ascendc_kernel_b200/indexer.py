@@ -214,6 +214,65 @@ class ModelNew(nn.Module):
         return out
 
 
+class KVCacheWriter(nn.Module):
+    """Producer of the compressed index-key cache that ``ModelNew`` reads
+    (reference/task2_v0_ref.py:119,133 read kv_cache[:bsz, :end_pos // ratio];
+    the reference holds no producer). After DeepSeek-V3.2-Exp's indexer key path
+    (inference/model.py, Indexer.forward: wk, LayerNorm ``k_norm``, RoPE), with the
+    rotary dims last as this reference's q and each block of ``compress_ratio``
+    tokens pooled by its mean (dsa_kv_cache_write)."""
+
+    def __init__(self, args, compress_ratio: int = 4):
+        super().__init__()
+        self.dim = args.dim
+        self.head_dim = args.index_head_dim
+        self.rope_head_dim = args.rope_head_dim
+        self.compress_ratio = compress_ratio
+        self.wk = Linear(self.dim, self.head_dim)
+        self.k_norm_weight = nn.Parameter(torch.ones(self.head_dim, dtype=torch.float32))
+        self.k_norm_bias = nn.Parameter(torch.zeros(self.head_dim, dtype=torch.float32))
+        self._dev_cache = {}
+
+    def _operands(self, freqs_cis: torch.Tensor, start_pos: int, seqlen: int, device):
+        """Device copies of wk, the LayerNorm affine and the RoPE tables, cached
+        until a parameter changes (the reference's weights live on the host)."""
+        vers = tuple((p._version, id(p), p.data_ptr())
+                     for p in (self.wk.weight, self.k_norm_weight, self.k_norm_bias))
+        key = (device, start_pos, seqlen, id(freqs_cis), vers)
+        c = self._dev_cache.get("ops")
+        if c is None or c[0] != key:
+            fc = torch.view_as_real(freqs_cis[start_pos:start_pos + seqlen])
+            c = (key,
+                 self.wk.weight.detach().to(device=device, dtype=torch.bfloat16).contiguous(),
+                 self.k_norm_weight.detach().to(device=device, dtype=torch.float32).contiguous(),
+                 self.k_norm_bias.detach().to(device=device, dtype=torch.float32).contiguous(),
+                 fc[..., 0].to(device=device, dtype=torch.float32).contiguous(),
+                 fc[..., 1].to(device=device, dtype=torch.float32).contiguous())
+            self._dev_cache["ops"] = c
+        return c[1:]
+
+    def forward(self, x: torch.Tensor, start_pos: int, freqs_cis: torch.Tensor,
+                kv_cache: torch.Tensor) -> torch.Tensor:
+        """Writes kv_cache[:bsz, start_pos // r : (start_pos + seqlen) // r] (complete
+        blocks of r = compress_ratio tokens; start_pos a multiple of r) and returns it."""
+        bsz, seqlen, _ = x.size()
+        r = self.compress_ratio
+        dev = x.device
+        assert x.is_cuda and x.dtype == torch.bfloat16 and kv_cache.dtype == torch.bfloat16
+        assert kv_cache.device == dev
+        assert kv_cache.stride(2) == 1 and kv_cache.stride(1) == self.head_dim
+        assert start_pos % r == 0, "start_pos must be a multiple of compress_ratio"
+        wk, g, b, cos, sin = self._operands(freqs_cis, start_pos, seqlen, dev)
+        x = x.contiguous()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            call("dsa_kv_cache_write", x.data_ptr(), wk.data_ptr(), g.data_ptr(), b.data_ptr(),
+                 cos.data_ptr(), sin.data_ptr(), kv_cache.data_ptr(), kv_cache.stride(0),
+                 kv_cache.shape[1], bsz, seqlen, self.dim, self.head_dim, self.rope_head_dim,
+                 start_pos, r, stream)
+        return kv_cache
+
+
 def qproj_rope(qr: torch.Tensor, wq: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                n_heads: int, head_dim: int, rope_dim: int, seqlen: int) -> torch.Tensor:
     """q = RoPE(bf16(qr @ wq.T)) with correctly rounded bf16 (dsa_indexer_qproj_rope).

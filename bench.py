@@ -561,6 +561,82 @@ def bench_chain(dev, cpu: bool):
     return res
 
 
+def bench_kv_writer(dev, cpu: bool):
+    """The compressed index-key cache of BASELINE configs[3]: x[4,16384,1024] ->
+    kv_cache[4,4096,64] (4:1). HBM roofline over x read once plus the written rows;
+    parity against the oracle on batch 0's first 1,024 tokens; the torch
+    restatement of the key path on the host cores on one batch, scaled to the call."""
+    import numpy as np
+    import torch
+
+    from ascendc_kernel_b200 import indexer as ix
+
+    b, s_len, dim, r = 4, 16384, 1024, 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    torch.manual_seed(7)
+    a = ix.ModelArgs(dim=dim, index_head_dim=64, rope_head_dim=32)
+    wr = ix.KVCacheWriter(a, r)
+    with torch.no_grad():
+        wr.k_norm_weight.copy_(1 + 0.1 * torch.randn(64))
+        wr.k_norm_bias.copy_(0.1 * torch.randn(64))
+    wr = wr.to(dev)
+    freqs = ix.make_freqs_cis(32, s_len)
+    x = torch.randn(b, s_len, dim, dtype=torch.bfloat16, device=dev, generator=gen)
+    kv = torch.zeros(b, s_len // r, 64, dtype=torch.bfloat16, device=dev)
+    wr(x, 0, freqs, kv)
+    us = cuda_timed(lambda: wr(x, 0, freqs, kv), 20) * 1e3
+    # the kernel alone through the C ABI (the module call adds host-side table set-up)
+    from ascendc_kernel_b200 import _native
+
+    fc = torch.view_as_real(freqs)
+    cos = fc[..., 0].to(dev).contiguous()
+    sin = fc[..., 1].to(dev).contiguous()
+    wk = wr.wk.weight.detach().contiguous()
+    g, bb = wr.k_norm_weight.detach(), wr.k_norm_bias.detach()
+    lib = _native.lib()
+
+    def raw():
+        lib.dsa_kv_cache_write(x.data_ptr(), wk.data_ptr(), g.data_ptr(), bb.data_ptr(),
+                               cos.data_ptr(), sin.data_ptr(), kv.data_ptr(), kv.stride(0),
+                               kv.shape[1], b, s_len, dim, 64, 32, 0, r,
+                               torch.cuda.current_stream(dev).cuda_stream)
+    k_us = graph_us(raw, reps=20)  # device time per launch, free of host launch overhead
+    nbytes = b * s_len * dim * 2 + 64 * dim * 2 + b * (s_len // r) * 64 * 2 + s_len * 16 * 4 * 2
+    flops = b * s_len * dim * 64 * 2
+    hbm, hbm_kind = load_peaks("hbm_gbs")
+    gbs = nbytes / (k_us * 1e-6) / 1e9
+    res = {"us_per_call": us, "kernel_us": k_us, "tokens_per_s": b * s_len / (us * 1e-6),
+           "roofline": {"bound": "hbm", "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
+                        "peak_gbs": hbm, "frac": gbs / hbm, "peak_source": hbm_kind,
+                        "algorithmic_flops": flops},
+           "shape": "x[4,16384,1024] -> kv_cache[4,4096,64], ratio 4, rope 32 (BASELINE "
+                    "configs[3]'s compressed cache)"}
+    import oracle
+
+    n = 1024
+    want = oracle.kv_writer(u16(x[:1, :n]), u16(wk), g.cpu().numpy(), bb.cpu().numpy(),
+                            fc[:n, :, 0].contiguous().numpy(), fc[:n, :, 1].contiguous().numpy(),
+                            np.zeros((1, n // r, 64), np.uint16), rope_dim=32, start_pos=0,
+                            ratio=r)
+    res["parity_vs_oracle"] = dict(bf16_parity(u16(kv[:1, :n // r]), want),
+                                   sample=f"batch 0, first {n} tokens ({n // r} rows)")
+    if cpu:
+        from oracle import v0_torch
+
+        xs = x[:1].cpu()
+        kc = torch.zeros(1, s_len // r, 64, dtype=torch.bfloat16)
+        wkc, gc, bc = wk.cpu(), g.cpu(), bb.cpu()
+        with torch.no_grad():
+            t, runs = cpu_timed(lambda: v0_torch.kv_writer_v32(xs, wkc, gc, bc, freqs, kc, 0, r,
+                                                               32), 4.0, max_runs=10)
+        res["cpu_baseline"] = {"value": t * b * 1e3, "unit": "ms/call", "cores": host_cores(),
+                               "kind": "port",
+                               "sample": f"batch 0 (16,384 tokens) x {runs} call(s), torch "
+                                         "restatement of the key path, scaled x4 to the call"}
+    return res
+
+
 def bench_host_link(dev, world, nbytes=256 << 20):
     """Pinned host<->device copy bandwidth of this rank's GPU with every rank copying
     at once: H2D alone, D2H alone and both directions together (GB/s per GPU, the
@@ -758,6 +834,10 @@ def run_ours(args, world, rank, local):
             others["chain"] = bench_chain(dev, cpu=(world == 1))
         except Exception as exc:
             others["chain"] = {"error": str(exc).splitlines()[0][:200]}
+        try:
+            others["kv_writer"] = bench_kv_writer(dev, cpu=(world == 1))
+        except Exception as exc:
+            others["kv_writer"] = {"error": str(exc).splitlines()[0][:200]}
     if rank == 0 and world == 1:
         import oracle
         from oracle import v0_torch
@@ -877,6 +957,23 @@ def run_profile_case(args):
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": "ix8", "batch": 8, "steps": args.warmup + args.steps}))
         return
+    if args.profile == "kvw":
+        # the kv_cache writer at configs[3]'s shape, batch args.batch (4: x 134 MB, larger
+        # than L2), W + K calls
+        from ascendc_kernel_b200 import indexer as ix
+
+        torch.manual_seed(7)
+        wr = ix.KVCacheWriter(ix.ModelArgs(dim=1024, index_head_dim=64, rope_head_dim=32),
+                              4).to(dev)
+        x = torch.randn(args.batch, 16384, 1024, dtype=torch.bfloat16, device=dev)
+        kv = torch.zeros(args.batch, 4096, 64, dtype=torch.bfloat16, device=dev)
+        freqs = ix.make_freqs_cis(32, 16384)
+        for _ in range(args.warmup + args.steps):
+            wr(x, 0, freqs, kv)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "kvw", "batch": args.batch,
+                          "steps": args.warmup + args.steps}))
+        return
     if args.profile in ("chain", "fchain"):
         # configs[3] at batch args.batch (1: ~0.9 GB on the device): indexer top-2048,
         # then the long-pool SparseAttention over its indices ("chain": two calls,
@@ -917,7 +1014,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--profile", choices=["sa", "ix", "ix8", "chain", "fchain", "sk"], default=None,
+    ap.add_argument("--profile", choices=["sa", "ix", "ix8", "kvw", "chain", "fchain", "sk"], default=None,
                     help="run only a bounded case of one kernel (for ncu)")
     ap.add_argument("--batch", type=int, default=4, help="batch of the --profile case")
     args = ap.parse_args()

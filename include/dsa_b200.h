@@ -230,6 +230,28 @@ int dsa_indexer_fwd_fp8(const void* x, const void* qr, const void* wq_b, const v
                         int64_t start_pos, int ratio, int64_t offset, float w_scale,
                         void* stream);
 
+/* ---- kv_cache writer: the producer of the compressed index-key cache that
+ * dsa_indexer_fwd reads (reference/task2_v0_ref.py:119,133 read
+ * kv_cache[:bsz, :end_pos // ratio]; the reference contains no producer).
+ * Definition after DeepSeek-V3.2-Exp's indexer key path (inference/model.py
+ * Indexer.forward: k = wk(x), LayerNorm, RoPE), the rotary dims last as this
+ * reference's q, and each block of `ratio` tokens pooled by its mean:
+ *   kl[t] = bf16(x[t] . wk^T)       (tensor cores, fp32 accumulation)
+ *   kn[t] = bf16(((kl - mean) * (1 / sqrt(var + 1e-6))) * ln_weight + ln_bias)
+ *   k[t]  = RoPE of kn's last rope_dim dims at position start_pos + t
+ *   kv_cache[b, start_pos / ratio + j] = bf16(mean_{i < ratio} k[j ratio + i])
+ * for the seqlen / ratio complete blocks (j = 0 .. seqlen / ratio - 1); other rows
+ * are untouched. x [batch*seqlen, dim] bf16, wk [head_dim, dim] bf16, ln_weight /
+ * ln_bias [head_dim] f32, cos/sin [seqlen, rope_dim/2] f32 (positions start_pos..),
+ * kv_cache rows of batch b at kv_cache + b*kv_batch_stride (kv_rows rows of
+ * head_dim). Supported: head_dim == 64, dim a multiple of 64, ratio dividing 128,
+ * start_pos a multiple of ratio. No counterpart in the reference (see above). */
+int dsa_kv_cache_write(const void* x, const void* wk, const float* ln_weight,
+                       const float* ln_bias, const float* cos_tab, const float* sin_tab,
+                       void* kv_cache, int64_t kv_batch_stride, int64_t kv_rows, int64_t batch,
+                       int64_t seqlen, int dim, int head_dim, int rope_dim, int64_t start_pos,
+                       int ratio, void* stream);
+
 /* dsa_indexer_fwd for callers that cannot allocate device memory at call
  * time -- plug-ins whose host framework owns all device memory and forbids
  * allocating inside an operator, or latency-critical paths where a

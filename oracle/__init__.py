@@ -39,6 +39,8 @@ _SIGS = {
     "oracle_index_topk": (None, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i32, _i32, _i64,
                                  _i32, _i64, _i32, _i64]),
     "oracle_e4m3_array": (None, [_vp, _i64, _vp]),
+    "oracle_kv_writer": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32,
+                                _i64, _i32]),
     "oracle_fp8_quant_rows": (None, [_vp, _i64, _vp, _vp]),
     "oracle_index_topk_fp8": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64,
                                      _i32, _i64, _i32, _i64]),
@@ -230,3 +232,21 @@ def indexer_fwd_fp8(x, qr, wq, wp, cos, sin, kv, *, n_heads, head_dim, rope_dim,
     if want_intermediates:
         return idx, {"q": q, "w": w, "q8": q8, "wq": wqs, "k8": k8, "ks": ks, "scores": scores}
     return idx
+
+
+# --------------------------------------------------------- kv_cache writer
+def kv_writer(x, wk, g, b, cos, sin, kv, *, rope_dim, start_pos, ratio):
+    """Writes the compressed index keys of x [B, S, dim] u16 into a copy of kv
+    [B, T, 64] u16 (entries start_pos/ratio .. start_pos/ratio + S/ratio - 1);
+    wk [64, dim] u16, g/b [64] f32, cos/sin [S, rope_dim/2] f32. Returns the copy."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    wk = np.ascontiguousarray(wk, dtype=np.uint16)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    cos = np.ascontiguousarray(cos, dtype=np.float32)
+    sin = np.ascontiguousarray(sin, dtype=np.float32)
+    out = np.array(kv, dtype=np.uint16, copy=True, order="C")
+    B, S, dim = x.shape
+    lib().oracle_kv_writer(_p(x), _p(wk), _p(g), _p(b), _p(cos), _p(sin), _p(out),
+                           out.shape[1] * 64, B, S, dim, rope_dim, start_pos, ratio)
+    return out

@@ -473,3 +473,64 @@ void oracle_index_topk_fp8(const uint8_t* q8, const float* wq, const uint8_t* k8
 void oracle_e4m3_array(const float* x, int64_t n, uint8_t* y) {
   for (int64_t i = 0; i < n; ++i) y[i] = oracle_e4m3_from_f32(x[i]);
 }
+
+/* --------------------------------------------------------- kv_cache writer
+ * Producer of the compressed cache the indexer reads (reference/task2_v0_ref.py:
+ * 119,133: kv_cache[:bsz, :end_pos // ratio], compress_ratio), which the
+ * reference itself does not contain. Restated from the indexer key path of
+ * DeepSeek-V3.2-Exp (inference/model.py, Indexer.forward: k = wk(x),
+ * k = k_norm(k) (LayerNorm, fp32, eps 1e-6), RoPE on the rotary dims, written to
+ * the cache at the token positions), with the rotary dims taken as the last
+ * rope_dim dims as this reference's q (reference/task2_v0_ref.py:131), and
+ * blocks of `ratio` consecutive tokens pooled by their mean (NSA-style block
+ * compression with a uniform map; ratio 1 writes every token as V3.2-Exp does):
+ *   kl[t]  = bf16(x[t] . wk^T)                       (correctly rounded)
+ *   mu     = fp32(sum_i kl_i) / 64, var = fp32(sum_i (kl_i - mu)^2) / 64
+ *                                                     (sequential, separately rounded)
+ *   kn_i   = bf16(((kl_i - mu) * (1 / sqrt(var + 1e-6))) * g_i + b_i)
+ *   k[t]   = RoPE of kn's last rope_dim dims at position start_pos + t (as
+ *            oracle_rope), bf16
+ *   cache[b, start_pos / ratio + j] = bf16(fp32(sum_{i<ratio} k[j ratio + i]) / ratio)
+ *            for every block j with (j + 1) ratio <= seqlen.
+ * x [B*S, dim] bf16, wk [64, dim] bf16, g/b [64] f32, cos/sin [S, rope_dim/2] f32,
+ * kv [B, ...] with batch stride kv_bstride elements.
+ */
+void oracle_kv_writer(const uint16_t* x, const uint16_t* wk, const float* g, const float* bta,
+                      const float* cos_t, const float* sin_t, uint16_t* kv, int64_t kv_bstride,
+                      int64_t B, int64_t S, int dim, int rope_dim, int64_t start_pos,
+                      int ratio) {
+  const int64_t rows = B * S;
+  uint16_t* keys = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)rows * 64);
+  oracle_linear_bf16(x, wk, keys, rows, dim, 64);
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    uint16_t* k = keys + r * 64;
+    float v[64];
+    float s = 0.0f;
+    for (int i = 0; i < 64; ++i) {
+      v[i] = bf2f(k[i]);
+      s += v[i];
+    }
+    const float mu = s / 64.0f;
+    float q = 0.0f;
+    for (int i = 0; i < 64; ++i) {
+      const float d = v[i] - mu;
+      q += d * d;
+    }
+    const float var = q / 64.0f;
+    const float rstd = 1.0f / sqrtf(var + 1e-6f);
+    for (int i = 0; i < 64; ++i) k[i] = f2bf(((v[i] - mu) * rstd) * g[i] + bta[i]);
+  }
+  oracle_rope(keys, cos_t, sin_t, rows, 1, 64, rope_dim, S);
+  const int64_t nblk = S / ratio;
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t j = 0; j < nblk; ++j) {
+      uint16_t* dst = kv + b * kv_bstride + (start_pos / ratio + j) * 64;
+      for (int d = 0; d < 64; ++d) {
+        float s = 0.0f;
+        for (int i = 0; i < ratio; ++i) s += bf2f(keys[(b * S + j * ratio + i) * 64 + d]);
+        dst[d] = f2bf(s / (float)ratio);
+      }
+    }
+  free(keys);
+}

@@ -83,6 +83,30 @@ def indexer_v0(wq_b: torch.Tensor, w_proj: torch.Tensor, freqs_cis: torch.Tensor
     return idx
 
 
+def kv_writer_v32(x: torch.Tensor, wk: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                  freqs_cis: torch.Tensor, kv_cache: torch.Tensor, start_pos: int, ratio: int,
+                  rope_dim: int) -> torch.Tensor:
+    """The compressed index-key cache the indexer reads (reference/task2_v0_ref.py:
+    119,133, kv_cache[:bsz, :end_pos // ratio]; the reference holds no producer),
+    after DeepSeek-V3.2-Exp's indexer key path (inference/model.py,
+    Indexer.forward: k = wk(x); k = k_norm(k), LayerNorm eps 1e-6 in fp32; RoPE),
+    with the rotary dims last as the reference's q (rotate_tail_ above) and each
+    block of `ratio` tokens pooled by its mean. x [b, s, dim] bf16, wk [64, dim]
+    bf16, gamma/beta [64] fp32, freqs_cis [max_seq, rope_dim/2] complex64. Returns
+    a copy of kv_cache with rows start_pos/ratio .. + s//ratio - 1 written."""
+    B, S, _ = x.shape
+    k = F.linear(x.double(), wk.double()).to(torch.bfloat16)
+    k = F.layer_norm(k.float(), (k.shape[-1],), gamma, beta, 1e-6).to(torch.bfloat16)
+    if rope_dim:
+        rotate_tail_(k.unsqueeze(2), freqs_cis[start_pos:start_pos + S], rope_dim)
+    nb = S // ratio
+    out = kv_cache.clone()
+    if nb:
+        pooled = k[:, :nb * ratio].float().view(B, nb, ratio, -1).mean(2).to(torch.bfloat16)
+        out[:, start_pos // ratio:start_pos // ratio + nb] = pooled
+    return out
+
+
 def sinkhorn_v0(x: torch.Tensor, repeat: int = 10, eps: float = 1e-6) -> torch.Tensor:
     """Model.forward of reference/task3_v0_ref.py:8-14."""
     y = x.softmax(-1) + eps

@@ -85,3 +85,35 @@ def test_sinkhorn_argument_checks(args, code):
 def test_error_carries_status_name():
     with pytest.raises(_native.DsaError, match="DSA_ERR_UNSUPPORTED"):
         _native.call("dsa_sinkhorn_fwd", FAKE, FAKE, 16, 5, 10, ctypes.c_float(1e-6), None)
+
+
+def kvw(**kw):
+    a = dict(x=FAKE, wk=FAKE, g=FAKE, b=FAKE, cos=FAKE, sin=FAKE, kv=FAKE, kvs=650 * 64,
+             rows=650, batch=8, s=2600, dim=1024, hd=64, rd=32, sp=0, r=4, stream=None)
+    a.update(kw)
+    return _native.lib().dsa_kv_cache_write(a["x"], a["wk"], a["g"], a["b"], a["cos"], a["sin"],
+                                            a["kv"], a["kvs"], a["rows"], a["batch"], a["s"],
+                                            a["dim"], a["hd"], a["rd"], a["sp"], a["r"],
+                                            a["stream"])
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(x=None), INVALID),
+    (dict(kv=None), INVALID),
+    (dict(cos=None), INVALID),            # rotary dims need the tables
+    (dict(rd=3), INVALID),                # odd rotary width
+    (dict(r=0), INVALID),
+    (dict(sp=2), INVALID),                # start_pos not a multiple of the ratio
+    (dict(rows=649), INVALID),            # the written blocks do not fit the cache
+    (dict(kvs=649 * 64), INVALID),        # batch stride shorter than the rows
+    (dict(hd=128), UNSUPPORTED),
+    (dict(dim=1000), UNSUPPORTED),
+    (dict(r=3), UNSUPPORTED),             # the ratio must divide the 128-token tile
+    (dict(x=FAKE + 2), MISALIGNED),
+    (dict(kvs=650 * 64 + 4), MISALIGNED),
+    (dict(batch=0), OK),                  # nothing to write
+    (dict(s=3), OK),                      # fewer tokens than one block
+    (dict(rd=0, cos=None, sin=None, batch=0), OK),
+])
+def test_kv_cache_write_argument_checks(kw, code):
+    assert kvw(**kw) == code
