@@ -314,30 +314,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int sg = __ldg(p.a_sig + m0 + r);
           const int a_span = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
           const bool any_order = a_span + __ldg(p.b_span + c) + log2k <= 53;
-          double acc64 = 0.0;
-          if (any_order) {
-            if (k0 < p.K) {
+          // the warp's sum of the exact fp64 products (each lane a 32-wide slice
+          // of k, then the lanes), and of their magnitudes: equal to the oracle's
+          // sequential sum when any order is exact, else certified against it
+          double acc64 = 0.0, mag64 = 0.0;
+          if (k0 < p.K) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t aw[4] = {av[j].x, av[j].y, av[j].z, av[j].w};
-                const uint32_t bw[4] = {bv[j].x, bv[j].y, bv[j].z, bv[j].w};
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t aw[4] = {av[j].x, av[j].y, av[j].z, av[j].w};
+              const uint32_t bw[4] = {bv[j].x, bv[j].y, bv[j].z, bv[j].w};
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  acc64 = fma(static_cast<double>(bf16lo_to_f32(aw[q])),
-                              static_cast<double>(bf16lo_to_f32(bw[q])), acc64);
-                  acc64 = fma(static_cast<double>(bf16hi_to_f32(aw[q])),
-                              static_cast<double>(bf16hi_to_f32(bw[q])), acc64);
-                }
+              for (int q = 0; q < 4; ++q) {
+                const double p0 = static_cast<double>(bf16lo_to_f32(aw[q])) *
+                                  static_cast<double>(bf16lo_to_f32(bw[q]));
+                const double p1 = static_cast<double>(bf16hi_to_f32(aw[q])) *
+                                  static_cast<double>(bf16hi_to_f32(bw[q]));
+                acc64 = __dadd_rn(acc64, p0);
+                acc64 = __dadd_rn(acc64, p1);
+                mag64 += fabs(p0) + fabs(p1);
               }
             }
+          }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc64 += __shfl_xor_sync(0xFFFFFFFFu, acc64, o);
-          } else if (lane == 0) {
+          for (int o = 16; o > 0; o >>= 1) {
+            acc64 += __shfl_xor_sync(0xFFFFFFFFu, acc64, o);
+            mag64 += __shfl_xor_sync(0xFFFFFFFFu, mag64, o);
+          }
+          uint32_t cert_bits;
+          if (!any_order && !certify_seq_dot_bf16(acc64, mag64, &cert_bits) && lane == 0) {
+            // the oracle's own chain: one lane, ascending k
+            acc64 = 0.0;
             for (int k8 = 0; k8 < p.K; k8 += 8) {
-              const uint4 av = __ldg(reinterpret_cast<const uint4*>(xr + k8));
-              const uint4 bv = __ldg(reinterpret_cast<const uint4*>(wr + k8));
-              const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+              const uint4 av8 = __ldg(reinterpret_cast<const uint4*>(xr + k8));
+              const uint4 bv8 = __ldg(reinterpret_cast<const uint4*>(wr + k8));
+              const uint32_t aw[4] = {av8.x, av8.y, av8.z, av8.w};
+              const uint32_t bw[4] = {bv8.x, bv8.y, bv8.z, bv8.w};
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 acc64 = fma(static_cast<double>(bf16lo_to_f32(aw[q])),

@@ -38,6 +38,24 @@ __device__ __forceinline__ uint32_t round_f64_to_bf16(double d) {
   return f32_to_bf16_rne(f);
 }
 
+// The CPU oracle rounds a dot product of bf16 inputs by summing the exact fp64
+// products in one sequential chain (ascending k) and rounding that sum
+// (round_f64_to_bf16). `sum` is the same products summed by a warp: each lane's
+// <= 32 terms in order, the lanes by a 5-step xor tree (every lane holds the
+// same bits); `mag` the same sum of |products|. Both chains lie within
+// (K - 1 + 36) 2^-53 mag (1 + 2^-40) of the exact value, so for K <= 1024 the
+// oracle's sum lies within 2^-42 mag of `sum`. When both ends of that interval
+// round to the same bf16 (monotone rounding), that is the oracle's result:
+// returns true and the bits; false sends the caller to the sequential chain.
+__device__ __forceinline__ bool certify_seq_dot_bf16(double sum, double mag, uint32_t* bits) {
+  const double bnd = mag * 0x1p-42;
+  if (!isfinite(sum) || !isfinite(bnd)) return false;
+  const uint32_t lo = round_f64_to_bf16(__dadd_rd(sum, -bnd));
+  const uint32_t hi = round_f64_to_bf16(__dadd_ru(sum, bnd));
+  *bits = lo;
+  return lo == hi;
+}
+
 // Certified rounding. v: fp32 approximation of an exact real x with
 // |v - x| <= E. Returns true and the bf16 bits of RNE(x) in *bits when that
 // can be decided from v alone, false when x may lie on the other side of a
