@@ -16,9 +16,10 @@
 // owns 128 TMEM columns and issues the tcgen05 MMAs (D[128 tokens x 64], four
 // K = 16 MMAs per chunk) into two accumulators, alternating tiles; warps 2-5 and
 // 6-9 are two epilogue warpgroups, one per accumulator (one token per thread:
-// the LayerNorm and RoPE chain, the key staged in the group's shared-memory
-// buffer, then the block means written as 16-byte rows), so each group has two
-// tiles' load time for one tile's chain. Roofline: HBM, x read once
+// the tile's RoPE factors staged in shared memory by coalesced loads while the
+// accumulator fills, the LayerNorm and RoPE chain, the key staged in the
+// group's shared-memory buffer, then the block means written as 16-byte rows),
+// so each group has two tiles' load time for one tile's chain. Roofline: HBM, x read once
 // (dim * 2 bytes per token), 128 / ratio bytes written per token.
 #include "common.cuh"
 #include "host_util.h"
@@ -38,7 +39,10 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kOffStage = 0;
 constexpr int kOffKeys = kStages * kStageBytes;        // [2 groups][128][64] bf16
 constexpr int kOffAffine = kOffKeys + 2 * kTile * kN * 2;  // LayerNorm weight, bias (f32)
-constexpr int kOffBar = kOffAffine + 2 * kN * 4;
+constexpr int kRopeStride = kN / 2 + 1;  // floats per token row of a staged table (odd: no bank conflicts)
+constexpr int kRopeTable = kTile * kRopeStride * 4;
+constexpr int kOffRope = kOffAffine + 2 * kN * 4;          // [2 groups][cos, sin][128][33] f32
+constexpr int kOffBar = kOffRope + 4 * kRopeTable;
 constexpr int kNumBars = 2 * kStages + 5;  // full, empty, acc_full[2], tmem_empty[2], done
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmem = kOffMisc + 16 + 1024;
@@ -50,6 +54,7 @@ struct Params {
   int tiles_per_batch;
   int dim;
   int rope_dim;
+  int rope_vec;  // RoPE tables 16-byte aligned with rope_dim / 2 a multiple of 4
   int ratio;
   int64_t entry0;      // start_pos / ratio
   int64_t kv_bstride;  // elements
@@ -187,9 +192,36 @@ __global__ void __launch_bounds__(kThreads, 1)
          tile += 2 * static_cast<int64_t>(gridDim.x), lt += 2) {
       const int64_t bi = tile / p.tiles_per_batch;
       const int64_t t0 = (tile % p.tiles_per_batch) * kTile;
+      // stage the tile's RoPE factors (coalesced rows [t0, t0 + 128) of the tables)
+      // while the accumulator fills; read back after the barrier below
+      float* rc = reinterpret_cast<float*>(smem + kOffRope + grp * 2 * kRopeTable);
+      float* rsn = rc + kTile * kRopeStride;
+      if (half > 0) {
+        const int64_t nv = p.S - t0 < kTile ? p.S - t0 : kTile;
+        const int nel = static_cast<int>(nv) * half;
+        const float* gc = p.cos_t + t0 * half;
+        const float* gsn = p.sin_t + t0 * half;
+        if (p.rope_vec) {  // 16-byte rows: float4 loads
+          for (int i = et; i < nel / 4; i += 128) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(gc) + i);
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(gsn) + i);
+            const int tok = (4 * i) / half, j = (4 * i) % half;
+            float* dc = rc + tok * kRopeStride + j;
+            float* ds = rsn + tok * kRopeStride + j;
+            dc[0] = c4.x; dc[1] = c4.y; dc[2] = c4.z; dc[3] = c4.w;
+            ds[0] = s4.x; ds[1] = s4.y; ds[2] = s4.z; ds[3] = s4.w;
+          }
+        } else {
+          for (int i = et; i < nel; i += 128) {
+            rc[(i / half) * kRopeStride + i % half] = __ldg(gc + i);
+            rsn[(i / half) * kRopeStride + i % half] = __ldg(gsn + i);
+          }
+        }
+      }
       bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[grp], (lt >> 1) & 1, abort_flag,
                                                   p.err, DSA_DEVERR_GEMM_WAIT));
-      // also orders this tile's key writes after every thread's reads of the last one
+      // also orders this tile's key writes after every thread's reads of the last one,
+      // and the staged RoPE factors before their reads
       if (!named_bar_and(bar_id, 128, ok)) break;
       tc_fence_after();
       uint32_t r0[32], r1[32];
@@ -243,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < kN / 2; ++j) {
         if (rope && 2 * j >= base) {
           const int jj = j - base / 2;
-          const float c = p.cos_t[t * half + jj], sn = p.sin_t[t * half + jj];
+          const float c = rc[row * kRopeStride + jj], sn = rsn[row * kRopeStride + jj];
           const float re = __uint_as_float(kb[j] << 16);
           const float im = __uint_as_float(kb[j] & 0xFFFF0000u);
           kb[j] = pack_bf16x2(__fsub_rn(__fmul_rn(re, c), __fmul_rn(im, sn)),
@@ -327,6 +359,7 @@ int launch_kv_writer(const void* x, const void* wk, const float* g, const float*
   p.ntiles = batch * p.tiles_per_batch;
   p.dim = dim;
   p.rope_dim = rope_dim;
+  p.rope_vec = (rope_dim % 8 == 0) && aligned16(cos_t) && aligned16(sin_t) ? 1 : 0;
   p.ratio = ratio;
   p.entry0 = start_pos / ratio;
   p.kv_bstride = kv_bstride;

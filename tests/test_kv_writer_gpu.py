@@ -69,6 +69,7 @@ CASES = [
     (3, 64, 256, 0, 0, 1, 70),        # ratio 1, no rotary dims
     (1, 130, 1024, 32, 16, 8, 40),    # ratio 8
     (1, 640, 2048, 32, 128, 128, 9),  # one block per 128-token tile
+    (2, 200, 512, 6, 4, 4, 60),       # 3 rotary pairs: tables staged with scalar loads
 ]
 
 
