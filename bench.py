@@ -54,6 +54,12 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # captured launch ends.
 SA_TRAFFIC_BYTES_PER_LAUNCH = 577_303_552
 
+# Warp-instructions one configs[2] launch of the indexer's score + top-k kernel executes
+# (ncu smsp__inst_executed.sum of the 6th launch of `--profile ix`: 110,332,893). The kernel
+# is bound by its CUDA-core chain, so its roofline is instruction issue: at most 4
+# warp-instructions per clock per SM (one per SM sub-partition).
+SCORE_WARP_INSTR = 110_332_893
+
 # BASELINE configs[2] (Lightning Indexer), per GPU
 IX_B, IX_S, IX_T, IX_K = 8, 2600, 650, 128
 
@@ -66,7 +72,8 @@ def load_peaks(key="hbm_gbs"):
             p = json.load(f)
         if key in p:
             return float(p[key]), "measured"
-    return (FALLBACK_HBM_GBS if key == "hbm_gbs" else FALLBACK_BF16_TFLOPS), "fallback"
+    fallback = {"hbm_gbs": FALLBACK_HBM_GBS, "sm_max_mhz": 1965.0}
+    return fallback.get(key, FALLBACK_BF16_TFLOPS), "fallback"
 
 
 def host_cores() -> int:
@@ -380,9 +387,17 @@ def bench_indexer(dev, world, cpu: bool):
     gbs = nbytes / (ms_local * 1e-3) / 1e9
     tfl = flops / (ms_local * 1e-3) / 1e12
     s_tfl = flops_score / (score_ms * 1e-3) / 1e12
+    sm_mhz, _ = load_peaks("sm_max_mhz")
+    props = torch.cuda.get_device_properties(dev)
+    issue_floor_us = SCORE_WARP_INSTR / (props.multi_processor_count * 4 * sm_mhz * 1e6) * 1e6
     res = {"n_gpus": world, "us_per_call": ms * 1e3,
            "tokens_per_s": world * IX_B * IX_S / (ms * 1e-3),
            "score_topk_kernel_us": score_ms * 1e3,
+           "score_kernel_issue_roofline": {
+               "bound": "instruction issue (CUDA cores)", "warp_instructions": SCORE_WARP_INSTR,
+               "floor_us": issue_floor_us, "frac": issue_floor_us / (score_ms * 1e3),
+               "floor": f"{SCORE_WARP_INSTR} warp-instructions / ({props.multi_processor_count} "
+                        f"SMs x 4 per clock x {sm_mhz:.0f} MHz)"},
            "roofline": {"bound": "mixed (CUDA-core certification chain)",
                         "algorithmic_bytes": nbytes, "algorithmic_flops": flops,
                         "achieved_gbs": gbs, "hbm_frac": gbs / hbm,
