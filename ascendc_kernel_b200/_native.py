@@ -40,6 +40,7 @@ SIGNATURES = {
                                       _c_void_p, _size_t, _c_void_p]),
     "dsa_indexer_score_workspace_bytes": (_size_t, [_i64, _i64, _i64, _i32]),
     "dsa_indexer_workspace_bytes": (_size_t, [_i64, _i64, _i32, _i32, _i64, _i32]),
+    "dsa_indexer_overlap_extra_bytes": (_size_t, [_i64, _i32, _i32]),
     "dsa_indexer_fwd": (_i32, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                _c_void_p, _i64, _c_void_p, _c_void_p, _size_t, _i64, _i64, _i32,
                                _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i64, _f32,

@@ -49,6 +49,9 @@ def indexer_sparse_attn(ix_model: "_ix.ModelNew", sa_model: "_sa.ModelNew", x: t
     cos, sin = ix_model._rope_tables(start_pos, seqlen, dev)
     sink = sa_model._sink_on(dev)
     nbytes = lib().dsa_chain_workspace_bytes(bsz, seqlen, ix_model.n_heads, ix_model.head_dim, T)
+    # room for a second projection scratch: the q and w projections run concurrently
+    nbytes += lib().dsa_indexer_overlap_extra_bytes(bsz * seqlen, ix_model.n_heads,
+                                                    ix_model.head_dim)
     ws = ix_model._workspace(nbytes, dev)
     if out is None:
         out = torch.empty_like(q)

@@ -1,6 +1,7 @@
 // Status strings, the per-device error word, device-info cache and the TMA
 // tensor-map encoder used by all entry points.
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -111,6 +112,37 @@ int set_func_attribute_once(const void* func, cudaFuncAttribute attr, int value)
   if (st != DSA_OK) return st;
   if (id == 0 && (st = current_context_id(&id)) != DSA_OK) return st;
   if (id != 0) ctx_store(id, func, tag, const_cast<void*>(func));
+  return DSA_OK;
+}
+
+namespace {
+thread_local std::vector<std::pair<unsigned long long, SideStream>> t_side_streams;
+}  // namespace
+
+int thread_side_stream(SideStream* out, bool may_create) {
+  unsigned long long id = 0;
+  int st = current_context_id(&id);
+  if (st != DSA_OK) return st;
+  if (id != 0)
+    for (const auto& e : t_side_streams)
+      if (e.first == id) {
+        *out = e.second;
+        return DSA_OK;
+      }
+  if (!may_create) return DSA_ERR_UNSUPPORTED;
+  SideStream s;
+  st = cuda_status(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+  if (st == DSA_OK) st = cuda_status(cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming));
+  if (st == DSA_OK) st = cuda_status(cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming));
+  if (st == DSA_OK && id == 0) st = current_context_id(&id);
+  if (st != DSA_OK || id == 0) {
+    if (s.join) cudaEventDestroy(s.join);
+    if (s.fork) cudaEventDestroy(s.fork);
+    if (s.stream) cudaStreamDestroy(s.stream);
+    return st != DSA_OK ? st : DSA_ERR_CUDA;
+  }
+  t_side_streams.emplace_back(id, s);
+  *out = s;
   return DSA_OK;
 }
 

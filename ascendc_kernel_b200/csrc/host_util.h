@@ -50,6 +50,21 @@ inline int set_max_dynamic_smem(const void* func, int bytes) {
   return set_func_attribute_once(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// A stream and a fork / join event pair of the calling thread in its current
+// context, created on first use and kept until the process exits (one set per
+// host thread, so concurrent callers never share a side stream). Entry points
+// use it to run two independent launch chains of one call concurrently: record
+// `fork` on the caller's stream, make `stream` wait on it, launch one chain on
+// `stream`, record `join` there and make the caller's stream wait on `join`.
+// With may_create false (the caller's stream is being captured into a CUDA
+// graph) a missing set is reported as DSA_ERR_UNSUPPORTED instead of created.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join = nullptr;
+};
+int thread_side_stream(SideStream* out, bool may_create);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace dsa

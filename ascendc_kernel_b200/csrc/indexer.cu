@@ -70,6 +70,11 @@ size_t front_bytes(int n_heads, int head_dim, int64_t rows) {
   return a > b ? a : b;
 }
 
+// Scratch of the q projection alone (slices, row data, fix-up bitmask).
+size_t qproj_scratch_bytes(int n_heads, int head_dim, int64_t rows) {
+  return align256(slice_region(n_heads, head_dim, rows).bytes);
+}
+
 // Slices wq_b and qr into the workspace, then runs the q projection.
 int run_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
               void* q_out, int64_t rows, int K, int n_heads, int head_dim, int rope_dim,
@@ -90,6 +95,47 @@ int run_qproj(const void* qr, const void* wq, const float* cos_tab, const float*
   return launch_qproj_rope(qr, wq, cos_tab, sin_tab, q_out, rows, K, n_heads, rope_dim, seqlen,
                            ws + r.a_slices, a_sig, a_err, a_n3, ws + r.b_slices, b_sig, b_err,
                            b_n3, b_span, reinterpret_cast<uint32_t*>(ws + r.open), s);
+}
+
+// The q projection (qr, wq_b -> q with RoPE) and the w projection (x, w_proj ->
+// w), which are independent until the scores. `front` holds either one's
+// scratch (front_bytes). With `extra` (qproj_scratch_bytes more, disjoint from
+// everything else) the w chain runs on the calling thread's side stream over
+// `front` while the q chain runs on `s` over `extra`, and `s` waits for both;
+// otherwise they run one after the other on `s` over `front`. Same results.
+int run_projections(const void* x, const void* qr, const void* wq_b, const void* w_proj,
+                    const float* cos_tab, const float* sin_tab, void* q, void* w, int64_t rows,
+                    int dim, int q_lora_rank, int n_heads, int head_dim, int rope_dim,
+                    int64_t seqlen, float w_scale, uint8_t* front, uint8_t* extra,
+                    cudaStream_t s) {
+  SideStream side;
+  bool overlap = extra != nullptr;
+  if (overlap) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const int st = cuda_status(cudaStreamIsCapturing(s, &cs));
+    if (st != DSA_OK) return st;
+    overlap = thread_side_stream(&side, cs == cudaStreamCaptureStatusNone) == DSA_OK;
+  }
+  if (!overlap) {
+    const int st = run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
+                             rope_dim, seqlen, front, s);
+    if (st != DSA_OK) return st;
+    return launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, front, s);
+  }
+  int st = cuda_status(cudaEventRecord(side.fork, s));
+  if (st == DSA_OK) st = cuda_status(cudaStreamWaitEvent(side.stream, side.fork, 0));
+  if (st != DSA_OK) return st;
+  const int st_w = launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, front, side.stream);
+  // the join is recorded and awaited even after a failed launch, so the side
+  // stream never leaves work (or a capture) behind
+  int st_j = cuda_status(cudaEventRecord(side.join, side.stream));
+  const int st_q = st_w != DSA_OK ? DSA_OK
+                                   : run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank,
+                                               n_heads, head_dim, rope_dim, seqlen, extra, s);
+  if (st_j == DSA_OK) st_j = cuda_status(cudaStreamWaitEvent(s, side.join, 0));
+  if (st_w != DSA_OK) return st_w;
+  if (st_q != DSA_OK) return st_q;
+  return st_j;
 }
 
 int check_qproj(const void* qr, const void* wq, const float* cos_tab, const float* sin_tab,
@@ -258,15 +304,20 @@ extern "C" int dsa_indexer_fwd(const void* x, const void* qr, const void* wq_b,
                         n_cand, topk, start_pos, ratio);
   if (st != DSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
-                      rope_dim, seqlen, ws, s);
-  if (st != DSA_OK) return st;
-  st = dsa::launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, ws, s);
+  // room after the layout for a second projection scratch: the projections overlap
+  const size_t extra = dsa::qproj_scratch_bytes(n_heads, head_dim, rows);
+  st = dsa::run_projections(x, qr, wq_b, w_proj, cos_tab, sin_tab, q, w, rows, dim, q_lora_rank,
+                            n_heads, head_dim, rope_dim, seqlen, w_scale, ws,
+                            workspace_bytes >= need + extra ? ws + need : nullptr, s);
   if (st != DSA_OK) return st;
   return dsa::run_score(q, w, kv_cache, kv_batch_stride, out, scores, batch, seqlen, n_cand, topk,
                         start_pos, ratio, offset, s);
 }
 
+extern "C" size_t dsa_indexer_overlap_extra_bytes(int64_t rows, int n_heads, int head_dim) {
+  if (rows <= 0 || n_heads <= 0 || head_dim <= 0) return 0;
+  return dsa::qproj_scratch_bytes(n_heads, head_dim, rows);
+}
 // ---------------------------------------------------------------- chained path
 namespace dsa {
 int launch_topk_mask(const void* scores, int64_t ld, uint32_t* mask, int words, int64_t batch,
@@ -341,10 +392,11 @@ extern "C" int dsa_chain_fwd(const void* x, const void* qr, const void* wq_b, co
                         batch, seqlen, ix_heads, ix_head_dim, n_cand, topk, start_pos, ratio);
   if (st != DSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, qi, rows, q_lora_rank, ix_heads, ix_head_dim,
-                      rope_dim, seqlen, ws + l.slices, s);
-  if (st != DSA_OK) return st;
-  st = dsa::launch_wproj_s8(x, w_proj, wi, rows, dim, w_scale, ws + l.slices, s);
+  const size_t extra = dsa::qproj_scratch_bytes(ix_heads, ix_head_dim, rows);
+  st = dsa::run_projections(x, qr, wq_b, w_proj, cos_tab, sin_tab, qi, wi, rows, dim,
+                            q_lora_rank, ix_heads, ix_head_dim, rope_dim, seqlen, w_scale,
+                            ws + l.slices,
+                            workspace_bytes >= l.bytes + extra ? ws + l.bytes : nullptr, s);
   if (st != DSA_OK) return st;
   st = dsa::launch_score_topk(qi, wi, kv_cache, kv_batch_stride, nullptr, scores, batch, seqlen,
                               n_cand, topk, start_pos, ratio, offset, s);
@@ -475,10 +527,10 @@ extern "C" int dsa_indexer_fwd_fp8(const void* x, const void* qr, const void* wq
                             start_pos, ratio);
   if (st != DSA_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  st = dsa::run_qproj(qr, wq_b, cos_tab, sin_tab, q, rows, q_lora_rank, n_heads, head_dim,
-                      rope_dim, seqlen, ws, s);
-  if (st != DSA_OK) return st;
-  st = dsa::launch_wproj_s8(x, w_proj, w, rows, dim, w_scale, ws, s);
+  const size_t extra = dsa::qproj_scratch_bytes(n_heads, head_dim, rows);
+  st = dsa::run_projections(x, qr, wq_b, w_proj, cos_tab, sin_tab, q, w, rows, dim, q_lora_rank,
+                            n_heads, head_dim, rope_dim, seqlen, w_scale, ws,
+                            workspace_bytes >= l.bytes + extra ? ws + l.bytes : nullptr, s);
   if (st != DSA_OK) return st;
   st = dsa::launch_fp8_quant_rows(q, rows * n_heads, rows * n_heads, 0, q8, nullptr, w, wq, s);
   if (st != DSA_OK) return st;

@@ -201,6 +201,8 @@ class ModelNew(nn.Module):
             nbytes = lib().dsa_indexer_workspace_bytes(bsz, seqlen, self.n_heads, self.head_dim,
                                                        T, K)
             fn = "dsa_indexer_fwd"
+        # room for a second projection scratch: the q and w projections run concurrently
+        nbytes += lib().dsa_indexer_overlap_extra_bytes(bsz * seqlen, self.n_heads, self.head_dim)
         ws = self._workspace(nbytes, dev)
         out = torch.empty(bsz, seqlen, K, dtype=torch.int64, device=dev)
         w_scale = self.softmax_scale * self.n_heads ** -0.5

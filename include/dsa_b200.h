@@ -168,9 +168,21 @@ size_t dsa_indexer_score_workspace_bytes(int64_t batch, int64_t seqlen, int64_t 
 size_t dsa_indexer_workspace_bytes(int64_t batch, int64_t seqlen, int n_heads, int head_dim,
                                    int64_t n_cand, int topk);
 
-/* (a)+(b)+(c) in one call on one stream. workspace must hold at least
+/* Extra workspace bytes that let dsa_indexer_fwd, dsa_indexer_fwd_fp8 and
+ * dsa_chain_fwd run the q projection (a) and the w projection (b), which are
+ * independent, concurrently: given at least their own workspace size plus this
+ * (rows = batch * seqlen), (b) runs on a side stream of the calling host thread
+ * (created on its first such call outside stream capture, kept until exit) and
+ * is joined back into the caller's stream before the scores; with no more than
+ * their own size they run one after the other. The results are identical either
+ * way. No counterpart in the reference (whose v1 overlaps its weights projection
+ * on a side stream of its own, src/task2_indexer.py:817-839). */
+size_t dsa_indexer_overlap_extra_bytes(int64_t rows, int n_heads, int head_dim);
+
+/* (a)+(b)+(c) in one call, ordered on `stream`. workspace must hold at least
  * dsa_indexer_workspace_bytes(batch, seqlen, n_heads, head_dim, n_cand, topk)
- * bytes, 256-byte aligned. cos/sin cover positions start_pos .. start_pos+seqlen-1.
+ * bytes, 256-byte aligned (plus dsa_indexer_overlap_extra_bytes to overlap (a)
+ * and (b)). cos/sin cover positions start_pos .. start_pos+seqlen-1.
  * n_cand = (start_pos + seqlen) / ratio; topk = min(index_topk, n_cand).
  * Replaces the whole ModelNew.forward path (src/task2_indexer.py:1056-1349),
  * semantics Model.forward in reference/task2_v0_ref.py:123-144. */

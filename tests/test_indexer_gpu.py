@@ -279,3 +279,75 @@ def test_full_reference_config(cuda_device):
     again = model(x.to(dev), qr.to(dev), start_pos, offset)
     assert torch.equal(got, again)
     assert _native.device_error(dev.index) == 0
+
+
+def _fwd_call(model, x, qr, ws, out, stream):
+    """dsa_indexer_fwd through the C ABI with the workspace `ws` (its size picks the
+    one-stream or the overlapped projections)."""
+    from ascendc_kernel_b200 import _native as nat
+
+    wq, wp = model._weights_on(x.device)
+    cos, sin = model._rope_tables(0, x.shape[1], x.device)
+    kv = model.kv_cache
+    return nat.lib().dsa_indexer_fwd(
+        x.data_ptr(), qr.data_ptr(), wq.data_ptr(), wp.data_ptr(), cos.data_ptr(),
+        sin.data_ptr(), kv.data_ptr(), kv.stride(0), out.data_ptr(), ws.data_ptr(), ws.numel(),
+        x.shape[0], x.shape[1], model.dim, model.q_lora_rank, model.n_heads, model.head_dim,
+        model.rope_head_dim, model.index_topk, 0, model.compress_ratio, 0,
+        float(model.softmax_scale * model.n_heads ** -0.5), stream)
+
+
+def test_overlapped_projections_equal_one_stream(cuda_device):
+    """The q and w projections on two streams (overlap workspace) give exactly the
+    indices of the one-stream order (minimum workspace), and those of ModelNew.forward."""
+    dev = cuda_device
+    torch.manual_seed(42)
+    args, freqs_cis, kv_cache, ratio = ix.get_init_inputs(device="cpu")
+    model = ix.ModelNew(args, freqs_cis.to(dev), kv_cache.to(dev), ratio)
+    x, qr, _, _ = ix.get_inputs(device="cpu")
+    x, qr = x[:2].to(dev), qr[:2].to(dev)
+    lib = _native.lib()
+    B, S, T, K = 2, x.shape[1], x.shape[1] // 4, args.index_topk
+    small = lib.dsa_indexer_workspace_bytes(B, S, 16, 64, T, K)
+    big = small + lib.dsa_indexer_overlap_extra_bytes(B * S, 16, 64)
+    assert big > small
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    outs = []
+    for nbytes in (small, big, big):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        out = torch.empty(B, S, K, dtype=torch.int64, device=dev)
+        assert _fwd_call(model, x, qr, ws, out, stream) == 0
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    assert torch.equal(outs[1].cpu(), model(x, qr, 0, 0).cpu())
+    assert _native.device_error(dev.index) == 0
+
+
+def test_overlapped_projections_in_a_cuda_graph(cuda_device):
+    """ModelNew.forward (overlap workspace) captured into a CUDA graph after one eager
+    call: the side stream forks from and joins back into the capture, and replays
+    reproduce the eager indices."""
+    dev = cuda_device
+    torch.manual_seed(42)
+    args, freqs_cis, kv_cache, ratio = ix.get_init_inputs(device="cpu")
+    model = ix.ModelNew(args, freqs_cis.to(dev), kv_cache.to(dev), ratio)
+    x, qr, _, _ = ix.get_inputs(device="cpu")
+    x, qr = x[:2].to(dev), qr[:2].to(dev)
+    want = model(x, qr, 0, 0).clone()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        model(x, qr, 0, 0)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        got = model(x, qr, 0, 0)
+    for _ in range(2):
+        got.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    del graph
+    assert _native.device_error(dev.index) == 0
