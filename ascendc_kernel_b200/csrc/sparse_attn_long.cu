@@ -7,36 +7,37 @@
 //   mx  = max(max_j s_j, sink[h])
 //   out = sum_j exp(s_j - mx) kv[b, idx_j] / (sum_j exp(s_j - mx) + exp(sink[h] - mx))
 // in the multiplicity form (c_k = #{j : idx_j == k}, sum_j f(idx_j) =
-// sum_k c_k f(k)), so the GEMMs stream contiguous 64-row chunks of kv[b]
+// sum_k c_k f(k)), so the GEMMs stream contiguous 128-row chunks of kv[b]
 // instead of gathering rows; chunks past the tile's largest index are skipped
 // (with causal indexer output that is about half of the pool on average).
 //
 // B200 mapping. A tile is 128 (token, head) rows (2 tokens of 64 heads, or 1 of
-// 128); a work item is two consecutive tiles of one batch, one per softmax
-// warpgroup, which share every kv chunk. Per CTA (one per SM, persistent):
-//   warp 0      TMA: kv chunks into a 4-stage ring (the first chunks of an item
-//               before its q tiles, so they arrive during the previous
-//               item's epilogue), the two q tiles.
+// 128); a work item is two consecutive tiles of one batch, which share every
+// 128-row kv chunk. Per CTA (one per SM, persistent, 384 threads):
+//   warp 0      TMA: kv chunks (128 rows x 128 dims, 32 KB) into a 2-stage ring
+//               (an item's first two chunks before its q tiles, so they arrive
+//               during the previous item's epilogue), the two q tiles.
 //   warp 1      tcgen05 issuer, per chunk and tile:
-//                 S[128 x 64]  = Q . KV_c^T              (8 x K16, smem operands)
-//                 O[128 x 128] += (P_hi + P_lo) . KV_c   (8 x K16, P read from TMEM)
-//               and releases a q tile as soon as its last S product completed.
-//   warps 2..9  two softmax warpgroups (tile 0 / tile 1 of the item). A thread
-//               owns one row. Per item the warpgroup turns the tile's counts
-//               into log2(c_k) per key; per chunk a thread reads S once, keeps
-//               a running max (O in TMEM is rescaled only when the max grows by
-//               more than 2^8), writes P = c_k 2^(z - m) back over S as two
-//               bf16 pieces (P_hi + P_lo carries ~16 bits), and after the last
-//               chunk divides O by the running sum plus the sink term and
-//               stores through the (then free) log2-count buffer.
+//                 S[128 x 128]  = Q . KV_c^T              (K-major smem operands)
+//                 O[128 x 128] += (P_hi + P_lo) . KV_c    (P read from TMEM, kv
+//                                                          as an MN-major operand)
+//               in the order PV(c) of a tile, then S(c+1) of the same tile into
+//               the columns PV(c) read, so one tile's softmax overlaps the other
+//               tile's products; a q tile is released once its last S completed.
+//   warps 2..9  softmax: both warpgroups serve both tiles; a thread owns one row
+//               and one half (64 keys) of every chunk: z = s scale log2(e) +
+//               log2(c_k) (-inf for c_k = 0), P = 2^(z - m) written back over S
+//               as two bf16 pieces (P_hi + P_lo carries ~16 bits). The two
+//               threads of a row agree the reference m through a 64-thread named
+//               barrier per TMEM lane quarter; it is set by the item's first
+//               chunk and moves (rescaling O and the sum) only when a chunk's max
+//               exceeds it by more than 2^32. After the last chunk O is divided
+//               by the sum plus the sink term and stored through the (then free)
+//               log2-count buffer.
 //   warps 10,11 count builders: the counts c_k of the NEXT item's tokens
 //               (shared-memory atomics on 16-bit counters) and its chunk
 //               count, while the current item computes.
-// Chunks are 64 kv rows. TMEM per warpgroup w: two S/P buffers at columns
-// [256w, 256w+64) and [256w+64, 256w+128), O at [256w+128, 256w+256). An S/P
-// buffer is reused two chunks later, once that chunk's PV product completed
-// (the issuer waits on its own commit), so QK^T of chunk c+1 overlaps the
-// softmax of chunk c.
+// TMEM per tile w: its S/P columns [256w, 256w+128) and O [256w+128, 256w+256).
 #include "common.cuh"
 #include "host_util.h"
 
