@@ -27,9 +27,10 @@
 //                          D[128 kv rows x 256 (token, head)] per 128-row kv
 //                          chunk (two K = 32 instructions), SWIZZLE_64B tiles by
 //                          TMA; an fp32 epilogue (relu, fma chain, * ks) that
-//                          stores orderable 32-bit keys in shared memory; top-K
-//                          per token in ten selection warps (warp_select.cuh),
-//                          joined between units by the four epilogue warps.
+//                          stores orderable 32-bit keys in shared memory (two
+//                          epilogue warpgroups); top-K per token in six
+//                          selection warps (warp_select.cuh), joined between
+//                          units by the eight epilogue warps.
 #include "common.cuh"
 #include "host_util.h"
 #include "numerics.cuh"
