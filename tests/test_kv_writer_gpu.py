@@ -105,6 +105,27 @@ def test_random_within_tolerance(cuda_device, case):
     assert np.array_equal(got[:, keep], to_u16(kv)[:, keep])
 
 
+@pytest.mark.parametrize("case", [
+    (1, 4, 64, 32, 0, 4, 1),      # one block, one 64-wide k chunk
+    (2, 3, 128, 32, 0, 4, 5),     # fewer tokens than a block: nothing written
+    (3, 7, 256, 32, 4, 4, 9),     # decode-sized call: one block per batch, a partial one left
+    (2, 128, 256, 64, 0, 128, 3), # one block of 128 tokens per batch
+])
+def test_small_and_degenerate_calls(cuda_device, case):
+    """Edge sizes: a single block, fewer tokens than a block (the cache is left as
+    it was), a decode-sized chunk, one 128-token block."""
+    B, S, dim, rd, sp, r, T = case
+    w = _writer(dim, rd, r, exact=True, seed=S + 7)
+    x, kv = _inputs(B, S, dim, T, exact=True, seed=S + 3)
+    freqs = ix.make_freqs_cis(rd, sp + S)
+    kvd = kv.to(cuda_device)
+    w.to(cuda_device)(x.to(cuda_device), sp, freqs, kvd)
+    assert np.array_equal(to_u16(kvd), _oracle(w.cpu(), x, kv, freqs, sp, rd, r))
+    if S < r:
+        assert np.array_equal(to_u16(kvd), to_u16(kv))
+    assert _native.device_error(0) == 0
+
+
 def test_chunked_prefill_equals_one_call(cuda_device):
     """Writing 512 tokens in two calls (start_pos 0 and 256) gives the same cache
     as one call over all 512: every block depends only on its own tokens and
