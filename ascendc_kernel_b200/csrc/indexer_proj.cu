@@ -236,18 +236,22 @@ __global__ void __launch_bounds__(kQThreads, 1)
               const uint64_t da2 = make_smem_desc(a2, 16u, 1024u, kLayoutSW128);
               const uint64_t da3 = make_smem_desc(a3, 16u, 1024u, kLayoutSW128);
               const uint64_t db123 = make_smem_desc(st + ko, 16u, 1024u, kLayoutSW128);
+              // The A3 product is issued between the other two: after the A2
+              // MMA (whose columns it overlaps entirely) the same work ran
+              // 1.4x slower, MMA-only. Integer sums: any order is exact.
               if (kb == 0 && step == 0) {
                 // first k step: every level's first writer overwrites it
                 const uint64_t db3 =
                     make_smem_desc(st + 2 * kQBBox + ko, 16u, 1024u, kLayoutSW128);
                 umma_s8(d + 0 * kQBN, da1, db123, idesc192, 0u);  // L2, L3, L4
                 umma_s8(d + 3 * kQBN, da2, db3, idesc64, 0u);     // L5
+                umma_s8(d + 2 * kQBN, da3, db123, idesc128, 1u);  // L4, L5
                 umma_s8(d + 1 * kQBN, da2, db123, idesc128, 1u);  // L3, L4
               } else {
                 umma_s8(d + 0 * kQBN, da1, db123, idesc192, 1u);  // L2, L3, L4
+                umma_s8(d + 2 * kQBN, da3, db123, idesc128, 1u);  // L4, L5
                 umma_s8(d + 1 * kQBN, da2, db123, idesc192, 1u);  // L3, L4, L5
               }
-              umma_s8(d + 2 * kQBN, da3, db123, idesc128, 1u);    // L4, L5
             }
             umma_commit(&b_empty[s]);
           }
@@ -325,23 +329,42 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const int ex_row = sa - 21 + 127;
       const uint32_t rsh = static_cast<uint32_t>(sa - 21) << 7;
       const int pos = static_cast<int>(static_cast<int64_t>(m0 + row) % p.seqlen);
-      for (int jn = 0; ok && jn < kQGroup; ++jn, ++g) {
-        const int nt = ng * kQGroup + jn;
-        if (nt >= p.n_tiles) break;
-        if ((g & 1) != wg) continue;
-        const int n0 = nt * kQBN;
-        const int* csig = csig_all + n0;
-        // RoPE tables of this row, fetched now, used after the conversion
-        float rc[kQRopeRegs], rs[kQRopeRegs];
-        if (rope_regs && row_valid) {
-          const float* ct = p.cos_tab + static_cast<int64_t>(pos) * half_rd;
-          const float* stt = p.sin_tab + static_cast<int64_t>(pos) * half_rd;
+      // RoPE tables of this row, once per unit (every head of it rotates the
+      // same row), 16-byte loads where the rows allow; loaded per head they
+      // cost the kernel 12 of its 64 us
+      float rc[kQRopeRegs], rs[kQRopeRegs];
+      if (rope_regs && row_valid) {
+        const float* ct = p.cos_tab + static_cast<int64_t>(pos) * half_rd;
+        const float* stt = p.sin_tab + static_cast<int64_t>(pos) * half_rd;
+        if (half_rd == kQRopeRegs &&
+            ((reinterpret_cast<uintptr_t>(ct) | reinterpret_cast<uintptr_t>(stt)) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < kQRopeRegs / 4; ++i) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(ct) + i);
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(stt) + i);
+            rc[4 * i] = c4.x;
+            rc[4 * i + 1] = c4.y;
+            rc[4 * i + 2] = c4.z;
+            rc[4 * i + 3] = c4.w;
+            rs[4 * i] = s4.x;
+            rs[4 * i + 1] = s4.y;
+            rs[4 * i + 2] = s4.z;
+            rs[4 * i + 3] = s4.w;
+          }
+        } else {
 #pragma unroll
           for (int i = 0; i < kQRopeRegs; ++i) {
             rc[i] = i < half_rd ? __ldg(ct + i) : 0.f;
             rs[i] = i < half_rd ? __ldg(stt + i) : 0.f;
           }
         }
+      }
+      for (int jn = 0; ok && jn < kQGroup; ++jn, ++g) {
+        const int nt = ng * kQGroup + jn;
+        if (nt >= p.n_tiles) break;
+        if ((g & 1) != wg) continue;
+        const int n0 = nt * kQBN;
+        const int* csig = csig_all + n0;
         // per (row, tile): error bound in units of T and the exponent range check
         const int sb_min = cext[nt * 4 + 0], sb_max = cext[nt * 4 + 1];
         const float eb_max = __int_as_float(cext[nt * 4 + 2]);
