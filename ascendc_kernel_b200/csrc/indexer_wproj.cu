@@ -180,18 +180,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t da2 = make_smem_desc(as + 1 * kABox + ko, 16u, 1024u, kLayoutSW128);
             const uint64_t da3 = make_smem_desc(as + 2 * kABox + ko, 16u, 1024u, kLayoutSW128);
             const uint64_t db123 = make_smem_desc(bs + ko, 16u, 1024u, kLayoutSW128);
+            // the A3 product between the other two, as in the q projection
+            // (after the A2 MMA, whose columns it overlaps, it stalls the pipe)
             if (kb == 0 && step == 0) {
               // first k step: every level's first writer overwrites it
               const uint64_t db3 = make_smem_desc(bs + 2 * kBN * 128 + ko, 16u, 1024u,
                                                   kLayoutSW128);
               umma_s8(d + 0 * kBN, da1, db123, idesc48, 0u);  // L2, L3, L4
               umma_s8(d + 3 * kBN, da2, db3, idesc16, 0u);    // L5
+              umma_s8(d + 2 * kBN, da3, db123, idesc32, 1u);  // L4, L5
               umma_s8(d + 1 * kBN, da2, db123, idesc32, 1u);  // L3, L4
             } else {
               umma_s8(d + 0 * kBN, da1, db123, idesc48, 1u);  // L2, L3, L4
+              umma_s8(d + 2 * kBN, da3, db123, idesc32, 1u);  // L4, L5
               umma_s8(d + 1 * kBN, da2, db123, idesc48, 1u);  // L3, L4, L5
             }
-            umma_s8(d + 2 * kBN, da3, db123, idesc32, 1u);    // L4, L5
           }
           umma_commit(&a_empty[s]);
         }
