@@ -445,7 +445,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int col = (c8_0 + j) * 8 + 2 * e;
-                  if (!((open >> col) & 1ull)) w4[e] = rope_pair(w4[e], rc[4 * j + e], rs[4 * j + e]);
+                  if (!((open >> col) & 1ull))
+                    w4[e] = rope_pair(w4[e], rc[4 * j + e], rs[4 * j + e]);
                 }
                 *addr = make_uint4(w4[0], w4[1], w4[2], w4[3]);
               }
@@ -500,6 +501,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
 // fp64 value. It is rounded once; a pair then gets its RoPE.
 constexpr int kFixWarps = 8;
 constexpr int kFixCap = 128;   // units per warp and round
+constexpr int kFixRowChunk = 256;  // rows a block scans at a time
+constexpr int kFixBlocksPerSm = 4;
 
 struct FixParams {
   int M;
@@ -575,100 +578,133 @@ __device__ __forceinline__ void fix_store(const FixParams& p, int row, int col, 
   }
 }
 
-__global__ void __launch_bounds__(kFixWarps * 32)
+__global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
     qproj_fixup_kernel(const FixParams p) {
   __shared__ uint16_t units[kFixWarps][kFixCap];
   __shared__ uint4 arow[kFixWarps][kQMaxK / 8];
+  __shared__ uint32_t row_seen[kFixRowChunk / 32];
+  __shared__ int row_list[kFixRowChunk];
+  __shared__ int n_list;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int words = p.N / 32;
   const int rope_c0 = kQBN - p.rope_dim;
   const int log2k = 32 - __clz(p.K - 1);  // ceil(log2 K)
   uint16_t* u = units[warp];
   uint4* a = arow[warp];
-  const int nwarps = gridDim.x * kFixWarps;
-  for (int row = blockIdx.x * kFixWarps + warp; row < p.M; row += nwarps) {
-    const uint32_t* ob = p.open_bits + static_cast<int64_t>(row) * words;
-    bool staged = false;
-    int span_a = 0;
-    for (int w0 = 0; w0 < words; w0 += 32) {
-      const uint32_t bits = (w0 + lane < words) ? __ldg(ob + w0 + lane) : 0u;
-      if (!__any_sync(0xFFFFFFFFu, bits != 0)) continue;
-      if (!staged) {
-        if (lane * 8 < p.K)
-          a[lane] = __ldg(reinterpret_cast<const uint4*>(p.qr + static_cast<int64_t>(row) * p.K) +
-                          lane);
-        // the row's bit span (sigma - lowest set bit), from the staged row
-        int low = 1 << 30;
-        if (lane * 8 < p.K) {
-          const uint4 v = a[lane];
-          low = min(min(bf16x2_low_bit(v.x), bf16x2_low_bit(v.y)),
-                    min(bf16x2_low_bit(v.z), bf16x2_low_bit(v.w)));
-        }
-        low = __reduce_min_sync(0xFFFFFFFFu, low);
-        const int sg = __ldg(p.a_sig + row);
-        span_a = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
-        staged = true;
-        __syncwarp();
-      }
-      // one unit per open non-rotated column and per open rotated pair (even column)
-      const int base = (w0 + lane) * 32;
-      const bool head_lo = (base % kQBN) == 0;  // the word holds head columns 0..31
-      const uint32_t rmask = head_lo ? (rope_c0 >= 32 ? 0u : (0xFFFFFFFFu << rope_c0))
-                                     : (rope_c0 >= 64 ? 0u
-                                        : rope_c0 >= 32 ? (0xFFFFFFFFu << (rope_c0 - 32))
-                                                        : 0xFFFFFFFFu);
-      uint32_t emit = (bits & ~rmask) | (bits & rmask & 0x55555555u);
-      while (__any_sync(0xFFFFFFFFu, emit != 0)) {
-        const int cnt = __popc(emit);
-        int incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if (lane >= o) incl += v;
-        }
-        const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
-        int w = incl - cnt;
-        while (emit && w < kFixCap) {
-          const int b = __ffs(emit) - 1;
-          emit &= emit - 1;
-          u[w++] = static_cast<uint16_t>(base + b);
-        }
-        __syncwarp();
-        const int n = total < kFixCap ? total : kFixCap;
-        // units whose dots are exact in any order: the whole warp, one by one
-        for (int i0 = 0; i0 < n; i0 += 32) {
-          const int my = i0 + lane;
-          bool ordered = false;
-          if (my < n) {
-            const int col = u[my];
-            const bool pair = (col % kQBN) >= rope_c0;
-            ordered = span_a + __ldg(p.b_span + col) + log2k > 53 ||
-                      (pair && span_a + __ldg(p.b_span + col + 1) + log2k > 53);
-          }
-          const uint32_t ord = __ballot_sync(0xFFFFFFFFu, ordered);
-          const int cnt_g = min(32, n - i0);
-          for (int j = 0; j < cnt_g; ++j) {
-            if ((ord >> j) & 1u) continue;
-            const int col = u[i0 + j];
-            const bool pair = (col % kQBN) >= rope_c0;
-            const uint16_t* b0 = p.wq + static_cast<int64_t>(col) * p.K;
-            const uint32_t v0 = round_f64_to_bf16(dot_f64_warp(a, b0, p.K, lane));
-            const uint32_t v1 = pair ? round_f64_to_bf16(dot_f64_warp(a, b0 + p.K, p.K, lane)) : 0u;
-            if (lane == 0) fix_store(p, row, col, pair, v0, v1, rope_c0);
-          }
-          // the others: one lane each, ascending k
-          if (ordered) {
-            const int col = u[my];
-            const bool pair = (col % kQBN) >= rope_c0;
-            const uint16_t* b0 = p.wq + static_cast<int64_t>(col) * p.K;
-            const uint32_t v0 = round_f64_to_bf16(dot_f64_seq(a, b0, p.K));
-            const uint32_t v1 = pair ? round_f64_to_bf16(dot_f64_seq(a, b0 + p.K, p.K)) : 0u;
-            fix_store(p, row, col, pair, v0, v1, rope_c0);
-          }
-        }
-        __syncwarp();
+  // The block owns a contiguous range of rows. Few rows have open elements, so
+  // the whole block first scans the range's bitmask (one round of coalesced
+  // loads) and lists those rows; each warp then takes listed rows, so that a
+  // row's chain of dependent loads (qr row, weight rows, RoPE tables) is not
+  // queued behind other rows' bitmask loads in the same warp.
+  const int per_block = static_cast<int>((p.M + gridDim.x - 1) / gridDim.x);
+  const int r_begin = blockIdx.x * per_block;
+  const int r_end = min(p.M, r_begin + per_block);
+  const int hwords = words / 2;  // one uint2 per head
+  for (int c0 = r_begin; c0 < r_end; c0 += kFixRowChunk) {
+    const int c1 = min(r_end, c0 + kFixRowChunk);
+    if (threadIdx.x < kFixRowChunk / 32) row_seen[threadIdx.x] = 0u;
+    if (threadIdx.x == 0) n_list = 0;
+    __syncthreads();
+    const uint2* ob2 =
+        reinterpret_cast<const uint2*>(p.open_bits + static_cast<int64_t>(c0) * words);
+    const int n2 = (c1 - c0) * hwords;
+    for (int i = threadIdx.x; i < n2; i += kFixWarps * 32) {
+      const uint2 v = __ldg(ob2 + i);
+      if ((v.x | v.y) != 0u) {
+        const int r = i / hwords;
+        const uint32_t bit = 1u << (r & 31);
+        if (!(atomicOr(&row_seen[r >> 5], bit) & bit)) row_list[atomicAdd(&n_list, 1)] = c0 + r;
       }
     }
+    __syncthreads();
+    const int n_rows = n_list;
+    for (int li = warp; li < n_rows; li += kFixWarps) {
+      const int row = row_list[li];
+      const uint32_t* ob = p.open_bits + static_cast<int64_t>(row) * words;
+      bool staged = false;
+      int span_a = 0;
+      for (int w0 = 0; w0 < words; w0 += 32) {
+        const uint32_t bits = (w0 + lane < words) ? __ldg(ob + w0 + lane) : 0u;
+        if (!__any_sync(0xFFFFFFFFu, bits != 0)) continue;
+        if (!staged) {
+          if (lane * 8 < p.K)
+            a[lane] = __ldg(reinterpret_cast<const uint4*>(p.qr + static_cast<int64_t>(row) * p.K) +
+                            lane);
+          // the row's bit span (sigma - lowest set bit), from the staged row
+          int low = 1 << 30;
+          if (lane * 8 < p.K) {
+            const uint4 v = a[lane];
+            low = min(min(bf16x2_low_bit(v.x), bf16x2_low_bit(v.y)),
+                      min(bf16x2_low_bit(v.z), bf16x2_low_bit(v.w)));
+          }
+          low = __reduce_min_sync(0xFFFFFFFFu, low);
+          const int sg = __ldg(p.a_sig + row);
+          span_a = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
+          staged = true;
+          __syncwarp();
+        }
+        // one unit per open non-rotated column and per open rotated pair (even column)
+        const int base = (w0 + lane) * 32;
+        const bool head_lo = (base % kQBN) == 0;  // the word holds head columns 0..31
+        const uint32_t rmask = head_lo ? (rope_c0 >= 32 ? 0u : (0xFFFFFFFFu << rope_c0))
+                                       : (rope_c0 >= 64 ? 0u
+                                          : rope_c0 >= 32 ? (0xFFFFFFFFu << (rope_c0 - 32))
+                                                          : 0xFFFFFFFFu);
+        uint32_t emit = (bits & ~rmask) | (bits & rmask & 0x55555555u);
+        while (__any_sync(0xFFFFFFFFu, emit != 0)) {
+          const int cnt = __popc(emit);
+          int incl = cnt;
+  #pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += v;
+          }
+          const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+          int w = incl - cnt;
+          while (emit && w < kFixCap) {
+            const int b = __ffs(emit) - 1;
+            emit &= emit - 1;
+            u[w++] = static_cast<uint16_t>(base + b);
+          }
+          __syncwarp();
+          const int n = total < kFixCap ? total : kFixCap;
+          // units whose dots are exact in any order: the whole warp, one by one
+          for (int i0 = 0; i0 < n; i0 += 32) {
+            const int my = i0 + lane;
+            bool ordered = false;
+            if (my < n) {
+              const int col = u[my];
+              const bool pair = (col % kQBN) >= rope_c0;
+              ordered = span_a + __ldg(p.b_span + col) + log2k > 53 ||
+                        (pair && span_a + __ldg(p.b_span + col + 1) + log2k > 53);
+            }
+            const uint32_t ord = __ballot_sync(0xFFFFFFFFu, ordered);
+            const int cnt_g = min(32, n - i0);
+            for (int j = 0; j < cnt_g; ++j) {
+              if ((ord >> j) & 1u) continue;
+              const int col = u[i0 + j];
+              const bool pair = (col % kQBN) >= rope_c0;
+              const uint16_t* b0 = p.wq + static_cast<int64_t>(col) * p.K;
+              const uint32_t v0 = round_f64_to_bf16(dot_f64_warp(a, b0, p.K, lane));
+              const uint32_t v1 =
+                  pair ? round_f64_to_bf16(dot_f64_warp(a, b0 + p.K, p.K, lane)) : 0u;
+              if (lane == 0) fix_store(p, row, col, pair, v0, v1, rope_c0);
+            }
+            // the others: one lane each, ascending k
+            if (ordered) {
+              const int col = u[my];
+              const bool pair = (col % kQBN) >= rope_c0;
+              const uint16_t* b0 = p.wq + static_cast<int64_t>(col) * p.K;
+              const uint32_t v0 = round_f64_to_bf16(dot_f64_seq(a, b0, p.K));
+              const uint32_t v1 = pair ? round_f64_to_bf16(dot_f64_seq(a, b0 + p.K, p.K)) : 0u;
+              fix_store(p, row, col, pair, v0, v1, rope_c0);
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -756,13 +792,14 @@ int launch_qproj_rope(const void* qr, const void* wq, const float* cos_tab, cons
   f.sin_tab = sin_tab;
   f.open_bits = open_bits;
   f.q = static_cast<uint16_t*>(q_out);
-  // shared memory first: the launch relies on 8 resident blocks per SM
+  // one wave: kFixBlocksPerSm resident blocks per SM (registers, shared memory)
   st = set_func_attribute_once(reinterpret_cast<const void*>(qproj_fixup_kernel),
                                cudaFuncAttributePreferredSharedMemoryCarveout,
                                cudaSharedmemCarveoutMaxShared);
   if (st != DSA_OK) return st;
   const int64_t fblocks = (rows + kFixWarps - 1) / kFixWarps;
-  const int64_t fgrid = fblocks < 8 * di.num_sms ? fblocks : 8 * di.num_sms;
+  const int64_t fmax = static_cast<int64_t>(kFixBlocksPerSm) * di.num_sms;
+  const int64_t fgrid = fblocks < fmax ? fblocks : fmax;
   qproj_fixup_kernel<<<static_cast<unsigned>(fgrid), kFixWarps * 32, 0, stream>>>(f);
   return cuda_status(cudaGetLastError());
 }
