@@ -137,9 +137,15 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, in
   }
 }
 
+// Resident blocks per SM the launch is compiled for: the sort is bound by the
+// latency of its shared-memory chains, so three blocks (40 registers a thread)
+// run it faster than two (64); n_cand > 4096 needs more registers.
+template <int J>
+constexpr int sort_blocks_per_sm() { return J <= 8 ? 3 : 1; }
+
 // J: step bound of this launch (n_cand <= kThreads * J).
 template <int J>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, sort_blocks_per_sm<J>())
     topk_sort_kernel(const Params p) {
   extern __shared__ uint32_t sm[];
   uint32_t* hist = sm;                       // [warps][256]
@@ -163,9 +169,13 @@ __global__ void __launch_bounds__(kThreads)
 template <int J>
 int launch_sort(const Params& p, const DeviceInfo& di, cudaStream_t stream) {
   const int smem = (kWarps * 256 + 32 + 2 * kThreads * J) * 4;
-  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(topk_sort_kernel<J>), smem);
+  int st = set_max_dynamic_smem(reinterpret_cast<const void*>(topk_sort_kernel<J>), smem);
   if (st != DSA_OK) return st;
-  int64_t grid = static_cast<int64_t>(di.num_sms) * 4;
+  st = set_func_attribute_once(reinterpret_cast<const void*>(topk_sort_kernel<J>),
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+  if (st != DSA_OK) return st;
+  int64_t grid = static_cast<int64_t>(di.num_sms) * sort_blocks_per_sm<J>();
   if (grid > p.rows) grid = p.rows;
   topk_sort_kernel<J><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(p);
   return cuda_status(cudaGetLastError());
