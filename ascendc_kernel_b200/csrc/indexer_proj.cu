@@ -454,16 +454,32 @@ __global__ void __launch_bounds__(kQThreads, 1)
           } else {
             const float* ct = p.cos_tab + static_cast<int64_t>(pos) * half_rd;
             const float* stt = p.sin_tab + static_cast<int64_t>(pos) * half_rd;
+            // a chunk's four pairs are four consecutive table entries: one
+            // 16-byte load of each table when the chunks and rows line up
+            const bool tab_vec =
+                (rope_c0 & 7) == 0 && (half_rd & 3) == 0 &&
+                ((reinterpret_cast<uintptr_t>(ct) | reinterpret_cast<uintptr_t>(stt)) & 15) == 0;
             for (int c8 = rope_c0 >> 3; c8 < (kQBN >> 3); ++c8) {
               uint4* addr = reinterpret_cast<uint4*>(stage + sw128_off(row, c8));
               uint4 v = *addr;
               uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+              if (tab_vec) {
+                const int pi0 = (c8 * 8 - rope_c0) >> 1;
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(ct + pi0));
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(stt + pi0));
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int col = c8 * 8 + 2 * e;
-                if (col < rope_c0 || ((open >> col) & 1ull)) continue;
-                const int pi = (col - rope_c0) >> 1;
-                w4[e] = rope_pair(w4[e], __ldg(ct + pi), __ldg(stt + pi));
+                for (int e = 0; e < 4; ++e)
+                  if (!((open >> (c8 * 8 + 2 * e)) & 1ull)) w4[e] = rope_pair(w4[e], cv[e], sv[e]);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int col = c8 * 8 + 2 * e;
+                  if (col < rope_c0 || ((open >> col) & 1ull)) continue;
+                  const int pi = (col - rope_c0) >> 1;
+                  w4[e] = rope_pair(w4[e], __ldg(ct + pi), __ldg(stt + pi));
+                }
               }
               *addr = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }

@@ -92,6 +92,28 @@ def test_qproj_slicing_edge_cases(cuda_device, k, mode):
     assert _native.device_error(dev.index) == 0
 
 
+@pytest.mark.parametrize("rd", [0, 2, 8, 20, 24, 48, 64])
+@pytest.mark.parametrize("n_heads", [16, 5])
+def test_qproj_rope_dims(cuda_device, rd, n_heads):
+    """RoPE widths other than the benchmark's 32: none, a single pair, rotated
+    columns that start inside a 16-byte chunk (20: column 44), tables held in
+    registers (8, 24, 32) or read per chunk (48, 64: every column rotated), and a
+    head count that is not a multiple of the 4-head work unit; bit-exact."""
+    gen = torch.Generator().manual_seed(rd * 3 + n_heads)
+    rows, seqlen, k = 300, 77, 256
+    qr = _edge_rows("wide", rows, k, gen)
+    wq = (torch.randn(n_heads * 64, k, generator=gen) * k ** -0.5).to(torch.bfloat16)
+    cos = torch.rand(seqlen, max(rd // 2, 1), generator=gen)[:, : rd // 2].contiguous()
+    sin = torch.rand(seqlen, max(rd // 2, 1), generator=gen)[:, : rd // 2].contiguous()
+    dev = cuda_device
+    q = ix.qproj_rope(qr.to(dev), wq.to(dev), cos.to(dev), sin.to(dev), n_heads, 64, rd, seqlen)
+    want = oracle.rope(oracle.linear_bf16(to_u16(qr), to_u16(wq)), cos.numpy(), sin.numpy(),
+                       n_heads, 64, rd, seqlen)
+    got = to_u16(q)
+    assert np.array_equal(got, want), int((got != want).sum())
+    assert _native.device_error(dev.index) == 0
+
+
 @pytest.mark.parametrize("k", [64, 512, 1024])
 @pytest.mark.parametrize("mode", ["normal", "wide", "special"])
 def test_wproj_edge_cases(cuda_device, k, mode):
