@@ -77,9 +77,11 @@ __device__ __forceinline__ void sort_row(const Params& p, int64_t row, int n, in
       if (j >= jr) break;
       const uint32_t d = 255u - ((v[j] >> shift) & 0xFFu);  // ascending digit = descending score
       const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
-      rank[j] = wh[d] + static_cast<uint32_t>(__popc(peers & lt_mask));
+      const uint32_t base = wh[d];
+      rank[j] = base + static_cast<uint32_t>(__popc(peers & lt_mask));
       __syncwarp();
-      if ((peers & lt_mask) == 0) wh[d] += static_cast<uint32_t>(__popc(peers));
+      // every lane of the digit stores the same new count: no divergent branch
+      wh[d] = base + static_cast<uint32_t>(__popc(peers));
       __syncwarp();
     }
     __syncthreads();
