@@ -579,16 +579,13 @@ __device__ __forceinline__ double dot_f64_warp(const uint4* a, const uint16_t* b
   return acc;
 }
 
+// rt: the row's RoPE tables (cos at [0, 32), sin at [32, 64)), staged with the row.
 __device__ __forceinline__ void fix_store(const FixParams& p, int row, int col, bool pair,
-                                          uint32_t v0, uint32_t v1, int rope_c0) {
+                                          uint32_t v0, uint32_t v1, int rope_c0, const float* rt) {
   uint16_t* dst = p.q + static_cast<int64_t>(row) * p.N + col;
   if (pair) {
-    const int half_rd = p.rope_dim / 2;
-    const int64_t pos = row % p.seqlen;
     const int pi = ((col % kQBN) - rope_c0) >> 1;
-    *reinterpret_cast<uint32_t*>(dst) =
-        rope_pair(v0 | (v1 << 16), __ldg(p.cos_tab + pos * half_rd + pi),
-                  __ldg(p.sin_tab + pos * half_rd + pi));
+    *reinterpret_cast<uint32_t*>(dst) = rope_pair(v0 | (v1 << 16), rt[pi], rt[32 + pi]);
   } else {
     *dst = static_cast<uint16_t>(v0);
   }
@@ -598,6 +595,7 @@ __global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
     qproj_fixup_kernel(const FixParams p) {
   __shared__ uint16_t units[kFixWarps][kFixCap];
   __shared__ uint4 arow[kFixWarps][kQMaxK / 8];
+  __shared__ float rtab[kFixWarps][64];  // the staged row's cos / sin (rope_dim <= 64)
   __shared__ uint32_t row_seen[kFixRowChunk / 32];
   __shared__ int row_list[kFixRowChunk];
   __shared__ int n_list;
@@ -643,9 +641,20 @@ __global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
         const uint32_t bits = (w0 + lane < words) ? __ldg(ob + w0 + lane) : 0u;
         if (!__any_sync(0xFFFFFFFFu, bits != 0)) continue;
         if (!staged) {
+          // the row, its exponent and its RoPE tables: independent loads, issued together
+          const int sg = __ldg(p.a_sig + row);
+          const int half_rd = p.rope_dim / 2;
+          const int64_t pos = row % p.seqlen;
+          float ct = 0.f, stb = 0.f;
+          if (lane < half_rd) {
+            ct = __ldg(p.cos_tab + pos * half_rd + lane);
+            stb = __ldg(p.sin_tab + pos * half_rd + lane);
+          }
           if (lane * 8 < p.K)
             a[lane] = __ldg(reinterpret_cast<const uint4*>(p.qr + static_cast<int64_t>(row) * p.K) +
                             lane);
+          rtab[warp][lane] = ct;
+          rtab[warp][32 + lane] = stb;
           // the row's bit span (sigma - lowest set bit), from the staged row
           int low = 1 << 30;
           if (lane * 8 < p.K) {
@@ -654,7 +663,6 @@ __global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
                       min(bf16x2_low_bit(v.z), bf16x2_low_bit(v.w)));
           }
           low = __reduce_min_sync(0xFFFFFFFFu, low);
-          const int sg = __ldg(p.a_sig + row);
           span_a = sg >= (1 << 20) ? (1 << 20) : (low == (1 << 30) ? 0 : sg - low);
           staged = true;
           __syncwarp();
@@ -704,7 +712,7 @@ __global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
               const uint32_t v0 = round_f64_to_bf16(dot_f64_warp(a, b0, p.K, lane));
               const uint32_t v1 =
                   pair ? round_f64_to_bf16(dot_f64_warp(a, b0 + p.K, p.K, lane)) : 0u;
-              if (lane == 0) fix_store(p, row, col, pair, v0, v1, rope_c0);
+              if (lane == 0) fix_store(p, row, col, pair, v0, v1, rope_c0, rtab[warp]);
             }
             // the others: one lane each, ascending k
             if (ordered) {
@@ -713,7 +721,7 @@ __global__ void __launch_bounds__(kFixWarps * 32, kFixBlocksPerSm)
               const uint16_t* b0 = p.wq + static_cast<int64_t>(col) * p.K;
               const uint32_t v0 = round_f64_to_bf16(dot_f64_seq(a, b0, p.K));
               const uint32_t v1 = pair ? round_f64_to_bf16(dot_f64_seq(a, b0 + p.K, p.K)) : 0u;
-              fix_store(p, row, col, pair, v0, v1, rope_c0);
+              fix_store(p, row, col, pair, v0, v1, rope_c0, rtab[warp]);
             }
           }
           __syncwarp();
